@@ -1,0 +1,498 @@
+"""Benchmark of the GIDS minibatch feature gather on B200.
+
+One step = one minibatch: the gather of the input-node features of one
+sampled minibatch (GIDS.fetch_feature's gather; the sampler is excluded, as
+in the reference's metric). Default workload: config 2 of the reference's
+benchmark table -- 100M-node homogeneous graph, fp32 x 1024 features
+(409.6 GB range), 4 KB pages striped over 4 emulated SSDs (ssd_list
+[0,1,2,3]), 40 GB GPU page cache, 3-layer fanout [15,10,5], batch 4096
+uniform seeds. Data is synthetic: features from the seeded generator, node
+ids from the seeded synthetic graph and sampler (GIDS/synthetic.py).
+
+The emulated SSDs hold `--phys-gb` GB of pages (default 64); logical page p
+is stored where page p mod (that many pages) is, so the 409.6 GB range, the
+cache behaviour and the host-link traffic are those of the full config while
+host RAM holds a fraction of it (the box has 196 GB of RAM).
+
+Timed regions (after --warmup steps, each bracketed by a barrier and a
+device synchronize, max over ranks):
+  value: K gathers with the node ids already in HBM (kernel path);
+  e2e:   K calls of GIDS.fetch_feature with the ids in pinned host memory
+         (H2D copy of the ids, gather, D2H read of one output element).
+Every step reads >= 13 GB, far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+Multi-GPU (torchrun): one process per GPU, each an independent
+data-parallel trainer with its own sampler seed (1000 + rank) and its own
+page cache; the emulated SSDs are one shared-memory copy mapped by every
+rank. NCCL only carries barriers and the max-over-ranks timing.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "gids-study_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: nodes, mean degree, zipf alpha, dim, dtype, page, ssds, cache MB, fanouts, batch, seed zipf
+    "c1": dict(nodes=1_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=1,
+               cache_mb=4096, fanouts=[10, 5], batch=1024, seed_zipf=None),
+    "c2": dict(nodes=100_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=4,
+               cache_mb=40 * 1024, fanouts=[15, 10, 5], batch=4096, seed_zipf=None),
+    "c4": dict(nodes=50_000_000, mean_deg=15, alpha=1.2, dim=768, dtype="float16", page=4096, ssds=4,
+               cache_mb=8 * 1024, fanouts=[10, 10], batch=2048, seed_zipf=1.0),
+    "c5": dict(nodes=500_000_000, mean_deg=10, alpha=1.1, dim=128, dtype="float32", page=4096, ssds=8,
+               cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None),
+}
+KIND = {"float32": 1, "float16": 2}
+TDTYPE = {"float32": torch.float32, "float16": torch.float16}
+ESIZE = {"float32": 4, "float16": 2}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ distributed
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend="nccl", device=None):
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            kw = dict(backend=backend, timeout=datetime.timedelta(seconds=600))
+            if backend == "nccl" and device is not None:
+                kw["device_id"] = device
+            dist.init_process_group(**kw)
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            if self.pg.get_backend() == "nccl":
+                self.pg.barrier(device_ids=[self.local])
+            else:
+                self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if self.pg is None:
+            return v
+        dev = torch.device("cuda", self.local) if self.pg.get_backend() == "nccl" else torch.device("cpu")
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if self.pg is None:
+            return v
+        dev = torch.device("cuda", self.local) if self.pg.get_backend() == "nccl" else torch.device("cpu")
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def sampler_seed(rank: int) -> int:
+    return 1000 + rank
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workload
+def make_batches(cfg, n_batches, rank, device):
+    """Input-node ids of n_batches minibatches from the seeded graph and sampler."""
+    from GIDS.synthetic import NeighborSampler, SyntheticGraph, seed_batches
+
+    t0 = time.time()
+    g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
+    s = NeighborSampler(g, cfg["fanouts"], seed=sampler_seed(rank))
+    seeds = seed_batches(cfg["nodes"], cfg["batch"], n_batches, sampler_seed(rank), device=device,
+                         zipf_alpha=cfg["seed_zipf"])
+    out = []
+    for sd in seeds:
+        inp, _ = s.sample(sd)
+        out.append(inp)
+    del g, s
+    if device != "cpu":
+        torch.cuda.synchronize()
+    return out, time.time() - t0
+
+
+def host_link_peak_gbs(device) -> float:
+    """Pinned host -> device copy bandwidth (GB/s), best of 3 x 1 GiB."""
+    n = 1 << 30
+    h = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(n, dtype=torch.uint8, device=device)
+    best = 0.0
+    for _ in range(4):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        d.copy_(h, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, n / 1e9 / (a.elapsed_time(b) / 1e3))
+    del h, d
+    return best
+
+
+def measured_hbm_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_mmap_gather(cfg, ids_list, seconds_budget, path_dir="/dev/shm", file_gb=8.0, warmup_ids=()):
+    """The reference's mmap baseline gather (torch.index_select on a np.memmap,
+    evaluation/dataloader.py:166-169 + homogenous_train_baseline.py:244),
+    timed on the host cores on a bounded sample of the same minibatches.
+    The memmap holds file_gb of rows; ids are taken modulo its row count."""
+    from oracle import oracle
+
+    dim, dt = cfg["dim"], cfg["dtype"]
+    row_bytes = dim * ESIZE[dt]
+    rows = max(1, min(cfg["nodes"], int(file_gb * 1e9) // row_bytes))
+    path = os.path.join(path_dir if os.path.isdir(path_dir) else "/tmp", f"gids_b200_mmap_{os.getpid()}.bin")
+    mm = np.memmap(path, dtype=np.dtype(dt), mode="w+", shape=(rows, dim))
+    oracle.synth_fill_into(KIND[dt], 1, 0, mm.reshape(-1))
+    mm.flush()
+    del mm
+    feat = oracle.open_memmap_table(path, np.dtype(dt), rows, dim)
+    try:
+        for ids in warmup_ids:
+            oracle.mmap_index_select(feat, torch.as_tensor(ids.cpu().numpy() % rows))
+        done_rows, t_total, n_batches = 0, 0.0, 0
+        for ids in ids_list:
+            ids_m = torch.as_tensor(ids.cpu().numpy() % rows)
+            t0 = time.perf_counter()
+            out = oracle.mmap_index_select(feat, ids_m)
+            t_total += time.perf_counter() - t0
+            done_rows += out.shape[0]
+            n_batches += 1
+            del out
+            if t_total >= seconds_budget:
+                break
+    finally:
+        del feat
+        os.unlink(path)
+    gbs = done_rows * row_bytes / 1e9 / t_total
+    return dict(value=gbs, unit="GB/s", cores=torch.get_num_threads(), kind="port",
+                minibatches_per_s=n_batches / t_total, seconds=t_total, steps=n_batches,
+                sample=f"{n_batches} minibatches ({done_rows} rows of {row_bytes} B) gathered by torch.index_select "
+                       f"from a {rows * row_bytes / 1e9:.1f} GB np.memmap in {path_dir} (ids mod {rows})")
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, cfg, dist: Dist):
+    import GIDS
+
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    dt, dim, page = cfg["dtype"], cfg["dim"], cfg["page"]
+    esize = ESIZE[dt]
+    row_bytes = dim * esize
+    num_ele = cfg["nodes"] * dim
+    range_bytes = num_ele * esize
+    phys = min(int(args.phys_gb * 1e9), range_bytes)
+    per_ssd = (phys // cfg["ssds"]) // page * page
+    shared = dist.world > 1
+    pattern = f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd{{}}" if shared else None
+
+    t0 = time.time()
+    if shared and dist.rank != 0:
+        dist.barrier()  # rank 0 creates and fills the shared emulated SSDs first
+    g = GIDS.GIDS(page_size=page, off=0, cache_dim=dim, num_ele=num_ele, num_ssd=cfg["ssds"],
+                  ssd_list=list(range(cfg["ssds"])), cache_size=cfg["cache_mb"], ctrl_idx=dist.local,
+                  dtype=TDTYPE[dt], ssd_capacity=per_ssd if phys < range_bytes else 0, ssd_path=pattern,
+                  synchronous=False)
+    t_store = time.time() - t0
+    t0 = time.time()
+    if not shared or dist.rank == 0:
+        g.BAM_FS.fill_synthetic(KIND[dt], 1, 0)
+    t_fill = time.time() - t0
+    if shared and dist.rank == 0:
+        dist.barrier()
+    geo = g.BAM_FS.geometry()
+    log(f"[rank {dist.rank}] store ready: {geo} (alloc {t_store:.1f}s, fill {t_fill:.1f}s)")
+
+    n_batches = args.warmup + 2 * args.steps
+    batches, t_sample = make_batches(cfg, n_batches, dist.rank, device)
+    sizes = [int(b.numel()) for b in batches]
+    log(f"[rank {dist.rank}] sampled {n_batches} minibatches in {t_sample:.1f}s, input nodes mean "
+        f"{np.mean(sizes):.0f}")
+    host_batches = [b.cpu().pin_memory() for b in batches]
+    out = torch.empty((max(sizes), dim), dtype=TDTYPE[dt], device=device)
+    stream = torch.cuda.current_stream(device)
+    sh = stream.cuda_stream
+    bam = g.BAM_FS
+
+    def gather_dev(ids):
+        bam.read_feature(out.data_ptr(), ids.data_ptr(), ids.numel(), dim, dim, 0, sh)
+
+    # warm-up (fills the cache)
+    for i in range(args.warmup):
+        gather_dev(batches[i])
+    torch.cuda.synchronize()
+    bam.reset_stats()
+
+    hbm_peak, hbm_src = measured_hbm_peak()
+    host_peak = host_link_peak_gbs(device) if dist.rank == 0 or True else 0.0
+
+    # ---- timed region 1: node ids resident in HBM
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    dev_ids = batches[args.warmup:args.warmup + args.steps]
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for ids in dev_ids:
+        gather_dev(ids)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t_val = ev0.elapsed_time(ev1) / 1e3
+    clk = clocks.stop()
+    st = bam.get_stats()
+    k_ms = bam.kernel_time_ms()
+    launches = st["launches"]
+    rows_val = sum(int(b.numel()) for b in dev_ids)
+
+    # ---- timed region 2: end to end through GIDS.fetch_feature, ids in pinned host memory
+    e2e_batches = host_batches[args.warmup + args.steps:]
+    it = iter([[b] for b in e2e_batches])
+    bam.reset_stats()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    checks = 0.0
+    for _ in e2e_batches:
+        batch = g.fetch_feature(dim, it, device)
+        checks += float(batch[-1][-1, -1].item())  # D2H read of the step's result
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall_e2e = time.perf_counter() - w0
+    dist.barrier()
+    t_e2e = e0.elapsed_time(e1) / 1e3
+    st_e2e = bam.get_stats()
+    rows_e2e = sum(int(b.numel()) for b in e2e_batches)
+
+    # ---- aggregate over ranks
+    t_val_max = dist.max(t_val)
+    t_e2e_max = dist.max(t_e2e)
+    rows_val_all = dist.sum(rows_val)
+    rows_e2e_all = dist.sum(rows_e2e)
+    steps_all = dist.sum(len(dev_ids))
+
+    # ---- mixed roofline of the gather kernel (per launch averages, this rank)
+    n_launch = max(1, launches)
+    t_launch = k_ms / 1e3 / n_launch
+    rows_l = st["rows"] / n_launch
+    r_host = (st["bytes_miss"] + st["bytes_bypass"] + st["bytes_cpu"]) / n_launch
+    r_hbm_src = st["bytes_hit"] / n_launch
+    alg_hbm = r_hbm_src + rows_l * row_bytes + 8 * rows_l  # source reads of hits + output writes + ids
+    t_star = max(alg_hbm / (hbm_peak * 1e9), r_host / (host_peak * 1e9))
+    bound = "hbm" if alg_hbm / (hbm_peak * 1e9) >= r_host / (host_peak * 1e9) else "host_link"
+    if bound == "hbm":
+        achieved, peak, unit_peak = alg_hbm / t_launch / 1e9, hbm_peak, "GB/s"
+    else:
+        achieved, peak, unit_peak = r_host / t_launch / 1e9, host_peak, "GB/s"
+    acc = max(1, st["access"])
+    roofline = {
+        "bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": unit_peak,
+        "frac": round(t_star / t_launch, 4), "traffic": None,
+        "peak_source": (hbm_src + " (of measured)") if bound == "hbm" else
+        "pinned host->device copy measured live in this run (of measured)",
+        "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss)/BW_host); frac = T*/T_launch",
+        "t_launch_ms": round(t_launch * 1e3, 3), "t_star_ms": round(t_star * 1e3, 3),
+        "hbm": {"alg_bytes_per_launch": int(alg_hbm), "achieved_gbs": round(alg_hbm / t_launch / 1e9, 1),
+                "peak_gbs": hbm_peak},
+        "host_link": {"alg_bytes_per_launch": int(r_host), "achieved_gbs": round(r_host / t_launch / 1e9, 2),
+                      "peak_gbs": round(host_peak, 2)},
+        "mix": {"hit": round(st["hit"] / acc, 4), "miss": round(st["miss"] / acc, 4),
+                "bypass": round(st["bypass"] / acc, 4), "cpu_rows": st["cpu_rows"]},
+    }
+    gb_val = rows_val_all * row_bytes / 1e9
+    value = gb_val / t_val_max
+    e2e_value = rows_e2e_all * row_bytes / 1e9 / t_e2e_max
+    result = {
+        "metric": "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs",
+        "value": round(value, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t_val_max / len(dev_ids) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt],
+        "data": "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)",
+        "minibatches_per_s": round(steps_all / t_val_max, 3),
+        "config": {"workload": f"{args.config}: {cfg['nodes']} nodes, {dt} x {dim} ({range_bytes / 1e9:.1f} GB range), "
+                               f"{page} B pages over {cfg['ssds']} emulated SSDs, {cfg['cache_mb'] // 1024} GB cache/GPU, "
+                               f"fanout {cfg['fanouts']}, batch {cfg['batch']}",
+                   "global_batch": cfg["batch"] * dist.world, "parallelism": f"dp{dist.world} (independent trainers)",
+                   "backing_store": {"logical_bytes": range_bytes, "physical_bytes": geo["wrap_pages"] * page,
+                                     "wrap_pages": geo["wrap_pages"]},
+                   "l2": "no flush: every step reads >= 13 GB (L2 is 126 MB)",
+                   "input_nodes_per_step": round(float(np.mean(sizes[args.warmup:args.warmup + args.steps])), 1)},
+        "roofline": roofline,
+        "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "api": "GIDS.fetch_feature",
+                "h2d_bytes_per_step": int(np.mean([b.numel() * 8 for b in e2e_batches])),
+                "d2h_bytes_per_step": esize, "wall_s": round(wall_e2e, 3),
+                "minibatches_per_s": round(dist.sum(len(e2e_batches)) / t_e2e_max, 3),
+                "mix": {"hit": round(st_e2e["hit"] / max(1, st_e2e["access"]), 4)}},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1)},
+    }
+    del out
+    torch.cuda.synchronize()
+    return result, batches
+
+
+def run_reference(args, cfg, dist: Dist):
+    """The reference's CPU gather (the mmap baseline) on the host cores."""
+    if dist.rank != 0:
+        return None
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    n = args.warmup + args.steps
+    batches, _ = make_batches(cfg, n, 0, dev)
+    batches = [b.cpu() for b in batches]
+    dt, dim = cfg["dtype"], cfg["dim"]
+    row_bytes = dim * ESIZE[dt]
+    # each step is one whole minibatch gathered by torch.index_select from the memmap
+    res = cpu_mmap_gather(cfg, batches[args.warmup:], 1e9, file_gb=args.cpu_file_gb,
+                          warmup_ids=batches[:args.warmup])
+    v = res["value"]
+    return {
+        "impl": "reference", "metric": "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs",
+        "value": round(v, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(res["seconds"] / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt], "data": "synthetic",
+        "minibatches_per_s": round(res["minibatches_per_s"], 3),
+        "config": {"workload": args.config, "global_batch": cfg["batch"], "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--phys-gb", type=float, default=64.0, help="GB of pages the emulated SSDs hold")
+    ap.add_argument("--cpu-file-gb", type=float, default=8.0, help="size of the CPU-baseline memmap")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--nodes", type=int, default=0, help="override the node count (small profiling cases)")
+    ap.add_argument("--cache-mb", type=int, default=0, help="override the cache size")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3")
+        args.warmup = 3
+    cfg = dict(CONFIGS[args.config])
+    if args.nodes:
+        cfg["nodes"] = args.nodes
+    if args.cache_mb:
+        cfg["cache_mb"] = args.cache_mb
+
+    dist = Dist()
+    if args.impl == "reference":
+        dist.init("gloo")
+        res = run_reference(args, cfg, dist)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        dist.close()
+        return
+
+    dist.init("nccl", torch.device("cuda", dist.local))
+    res, batches = run_ours(args, cfg, dist)
+    if dist.rank == 0 and dist.world == 1:
+        res["cpu_baseline"] = cpu_mmap_gather(cfg, batches, args.cpu_seconds, file_gb=args.cpu_file_gb)
+    if dist.rank == 0:
+        print(json.dumps(res), flush=True)
+    dist.barrier()
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

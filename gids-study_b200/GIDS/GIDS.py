@@ -1,0 +1,371 @@
+"""GIDS Python API on the B200 feature store.
+
+Drop-in for GIDS_Setup/GIDS/GIDS.py of the reference: the ``GIDS`` class keeps
+its constructor keywords, its methods and the semantics of ``fetch_feature``
+(window buffering, Storage Access Accumulator, heterograph key offsets), and
+``GIDS_DGLDataLoader`` keeps its signature. Feature gathers run in the CUDA
+library behind the ``BAM_Feature_Store`` module; nothing here touches feature
+data on the CPU.
+
+Differences from the reference, all of which leave the gathered values
+unchanged:
+* the output tensor has the store's element type (the reference always
+  allocates float32, GIDS.py:908,961,1017,1046, which is wrong for
+  ``long_type``) and is allocated with ``torch.empty`` (every element is
+  written by the gather);
+* gathers are stream-ordered on the current torch stream instead of ending in
+  a device-wide synchronize (pass ``synchronous=True`` for the old behaviour);
+* the store lives on ``cuda:ctrl_idx`` (the reference hard-wires device 0,
+  bam_nvme.h:135,293);
+* a heterograph type with an empty id list is skipped (the reference's
+  ``next`` there is a no-op, GIDS.py:717-719).
+"""
+from __future__ import annotations
+
+import math
+import time
+from collections.abc import Mapping
+
+import torch
+
+import BAM_Feature_Store
+
+_STORE_CLASSES = {
+    torch.float32: BAM_Feature_Store.BAM_Feature_Store_float,
+    torch.int64: BAM_Feature_Store.BAM_Feature_Store_long,
+    torch.float16: BAM_Feature_Store.BAM_Feature_Store_half,
+    torch.bfloat16: BAM_Feature_Store.BAM_Feature_Store_bfloat16,
+}
+
+
+def _current_stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _as_index(v, device) -> torch.Tensor:
+    t = v if isinstance(v, torch.Tensor) else torch.as_tensor(v)
+    if t.dtype != torch.int64:
+        t = t.to(torch.int64)
+    return t.to(device, non_blocking=True).contiguous()
+
+
+def _with_features(batch, feat):
+    """Append the gathered features to a sampler batch (GIDS.py:1029-1034, 1053-1058)."""
+    if isinstance(batch, tuple):
+        return (*batch, feat)
+    batch.append(feat)
+    return batch
+
+
+class GIDS:
+    """Feature fetcher over the GPU page cache (GIDS.py:490-1128).
+
+    Constructor keywords and defaults follow GIDS.py:510-517. Keyword-only
+    extensions: ``dtype`` (feature element type; default float32, int64 with
+    ``long_type``), ``ssd_capacity`` (bytes held per emulated SSD, 0 = the
+    whole stripe; smaller values wrap), ``ssd_path`` (file pattern such as
+    ``/dev/shm/gids_ssd{}`` for emulated SSDs shared across processes) and
+    ``synchronous``.
+    """
+
+    def __init__(self, page_size=4096, off=0, cache_dim=1024, num_ele=300 * 1000 * 1000 * 1024, num_ssd=1,
+                 ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
+                 long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
+                 ssd_path=None, synchronous=False):
+        if dtype is None:
+            dtype = torch.int64 if long_type else torch.float32
+        if dtype not in _STORE_CLASSES:
+            raise ValueError(f"unsupported feature dtype {dtype}")
+        self.dtype = dtype
+        self.BAM_FS = _STORE_CLASSES[dtype]()
+
+        self.accumulator_flag = accumulator_flag
+        self.required_accesses = 0
+        self.prev_cpu_access = 0
+        self.return_torch_buffer = []
+        self.index_list = []
+
+        self.window_buffering_flag = window_buffer
+        self.window_buffer = []
+        self.wb_init = False
+        self.wb_size = wb_size
+
+        self.page_size = page_size
+        # byte offset -> first page on every SSD (GIDS.py:583)
+        self.off = math.ceil(math.ceil(off / page_size) / num_ssd)
+        self.num_ele = num_ele
+        self.cache_size = cache_size
+        self.heterograph = heterograph
+        self.heterograph_map = heterograph_map
+        self.graph_GIDS = None
+        self.cache_dim = cache_dim
+        self.gids_device = "cuda:" + str(ctrl_idx)
+        self.device = torch.device(self.gids_device)
+
+        self.GIDS_controller = BAM_Feature_Store.GIDS_Controllers()
+        if ssd_list is None:
+            print("SSD are not assigned")
+            self.ssd_list = [i for i in range(num_ssd)]
+        else:
+            self.ssd_list = ssd_list
+        print("ssd list: ", ssd_list)
+        self.GIDS_controller.init_GIDS_controllers(num_ssd, 1024, 128, self.ssd_list)
+        if ssd_capacity or ssd_path:
+            self.GIDS_controller.set_emulation(int(ssd_capacity or 0), ssd_path or "")
+
+        self.BAM_FS.set_device(ctrl_idx)
+        self.BAM_FS.init_controllers(self.GIDS_controller, page_size, self.off, cache_size, num_ele, num_ssd)
+        self.BAM_FS.set_row_layout(cache_dim)
+        self.BAM_FS.set_synchronous(bool(synchronous))
+        self.synchronous = bool(synchronous)
+
+        self.GIDS_time = 0.0
+        self.WB_time = 0.0
+
+    # ------------------------------------------------------------ out of scope
+    def init_graph_GIDS(self, page_size, off, cache_size, num_ele, num_ssd):
+        """Graph-structure-on-SSD sampling (GIDS.py:636-650) is not implemented."""
+        raise NotImplementedError("graph-structure sampling from storage is not part of this library")
+
+    def get_offset_array(self):
+        raise NotImplementedError("graph-structure sampling from storage is not part of this library")
+
+    def get_array_ptr(self):
+        raise NotImplementedError("graph-structure sampling from storage is not part of this library")
+
+    # ------------------------------------------------------ constant CPU buffer
+    def cpu_backing_buffer(self, dim, length):
+        """Allocate the pinned constant CPU buffer (GIDS.py:667-678)."""
+        self.BAM_FS.cpu_backing_buffer(dim, length)
+
+    def set_cpu_buffer(self, ten, N):
+        """Pin the first N node ids of ``ten`` (a pin_file list, GIDS.py:680-699)."""
+        topk_ten = torch.as_tensor(ten)[:N]
+        topk_len = len(topk_ten)
+        d_ten = topk_ten.to(torch.int64).to(self.device).contiguous()
+        self.BAM_FS.set_cpu_buffer(d_ten.data_ptr(), topk_len)
+
+    # ------------------------------------------------------- window buffering
+    def window_buffering(self, batch):
+        """Protect the pages of an upcoming batch from eviction (GIDS.py:702-748)."""
+        s_time = time.time()
+        stream = _current_stream_handle(self.device)
+        if self.heterograph:
+            for key, value in batch[0].items():
+                if len(value) == 0:
+                    continue
+                input_tensor = _as_index(value, self.device)
+                key_off = 0
+                if self.heterograph_map is not None:
+                    if key in self.heterograph_map:
+                        key_off = self.heterograph_map[key]
+                    else:
+                        print("Cannot find key: ", key, " in the heterograph map!")
+                self.BAM_FS.set_window_buffering(input_tensor.data_ptr(), len(input_tensor), int(key_off), stream)
+        else:
+            input_tensor = _as_index(batch[0], self.device)
+            self.BAM_FS.set_window_buffering(input_tensor.data_ptr(), len(input_tensor), 0, stream)
+        self.WB_time += time.time() - s_time
+
+    def fill_wb(self, it, num):
+        """Pull ``num`` batches ahead and mark them (GIDS.py:752-769)."""
+        for _ in range(num):
+            batch = next(it)
+            self.window_buffer.append(batch)
+            self.window_buffering(batch)
+
+    # ----------------------------------------------- storage access accumulator
+    def set_required_storage_access(self, bw, l_ssd, l_system, num_ssd, p):
+        """Accesses needed to keep the SSDs at fraction p of peak (GIDS.py:773-788)."""
+        accesses = (p * bw * 1024 / self.page_size * (l_ssd + l_system) * num_ssd) / (1 - p)
+        self.required_accesses = accesses
+        print("Number of required storage accesses: ", accesses)
+
+    # ------------------------------------------------------------ the gather
+    def _new_out(self, n, dim):
+        return torch.empty((n, dim), dtype=self.dtype, device=self.device)
+
+    def _key_off(self, key):
+        if self.heterograph_map is not None:
+            if key in self.heterograph_map:
+                return int(self.heterograph_map[key])
+            print("Cannot find key: ", key, " in the heterograph map!")
+        return 0
+
+    def fetch_feature(self, dim, it, device):
+        """Next batch from ``it`` with its gathered features appended (GIDS.py:791-1058)."""
+        GIDS_time_start = time.time()
+        stream = _current_stream_handle(self.device)
+
+        if self.window_buffering_flag and not self.wb_init:
+            self.fill_wb(it, self.wb_size)
+            self.wb_init = True
+
+        next_batch = next(it)
+        self.window_buffer.append(next_batch)
+        if self.window_buffering_flag:
+            self.window_buffering(next_batch)
+
+        if self.accumulator_flag:
+            return self._fetch_accumulated(dim, it, stream, GIDS_time_start)
+
+        batch = self.window_buffer.pop(0)
+        if self.heterograph:
+            ret_ten, outs, idxs, ns, keys = {}, [], [], [], []
+            for key, v in batch[0].items():
+                if len(v) == 0:
+                    ret_ten[key] = self._new_out(0, dim)
+                    continue
+                g_index = _as_index(v, self.device)
+                out = self._new_out(len(g_index), dim)
+                ret_ten[key] = out
+                outs.append(out.data_ptr())
+                idxs.append(g_index.data_ptr())
+                ns.append(len(g_index))
+                keys.append(self._key_off(key))
+            self.BAM_FS.read_feature_hetero(len(outs), outs, idxs, ns, dim, self.cache_dim, keys, stream)
+            self.GIDS_time += time.time() - GIDS_time_start
+            return _with_features(batch, ret_ten)
+
+        index = _as_index(batch[0], self.device)
+        out = self._new_out(len(index), dim)
+        self.BAM_FS.read_feature(out.data_ptr(), index.data_ptr(), len(index), dim, self.cache_dim, 0, stream)
+        self.GIDS_time += time.time() - GIDS_time_start
+        return _with_features(batch, out)
+
+    def _fetch_accumulated(self, dim, it, stream, t0):
+        """Storage Access Accumulator (GIDS.py:836-984): gather enough queued
+        batches in one launch to keep the storage busy, hand them out one per call."""
+        if len(self.return_torch_buffer) != 0:
+            return_ten = self.return_torch_buffer.pop(0)
+            return_batch = self.window_buffer.pop(0)
+            self.GIDS_time += time.time() - t0
+            return _with_features(return_batch, return_ten)
+
+        def n_access(b):
+            if self.heterograph:
+                return sum(len(v) for v in b[0].values())
+            return len(b[0])
+
+        buffer_size = len(self.window_buffer)
+        current_access = 0
+        num_iter = 0
+        required_accesses = self.required_accesses
+        while True:
+            if num_iter >= buffer_size:
+                batch = next(it)
+                self.window_buffer.append(batch)
+                if self.window_buffering_flag:
+                    self.window_buffering(batch)
+            else:
+                batch = self.window_buffer[num_iter]
+            current_access += n_access(batch)
+            num_iter += 1
+            required_accesses += self.prev_cpu_access
+            if current_access > required_accesses:
+                break
+
+        outs, idxs, ns, keys = [], [], [], []
+        keep_alive = []
+        for i in range(num_iter):
+            batch = self.window_buffer[i]
+            if self.heterograph:
+                ret_ten = {}
+                for k, v in batch[0].items():
+                    if len(v) == 0:
+                        ret_ten[k] = self._new_out(0, dim)
+                        continue
+                    g_index = _as_index(v, self.device)
+                    keep_alive.append(g_index)
+                    out = self._new_out(len(g_index), dim)
+                    ret_ten[k] = out
+                    outs.append(out.data_ptr())
+                    idxs.append(g_index.data_ptr())
+                    ns.append(len(g_index))
+                    keys.append(self._key_off(k))
+                self.return_torch_buffer.append(ret_ten)
+            else:
+                g_index = _as_index(batch[0], self.device)
+                keep_alive.append(g_index)
+                out = self._new_out(len(g_index), dim)
+                outs.append(out.data_ptr())
+                idxs.append(g_index.data_ptr())
+                ns.append(len(g_index))
+                keys.append(0)
+                self.return_torch_buffer.append(out)
+        if self.heterograph:
+            self.BAM_FS.read_feature_merged_hetero(len(outs), outs, idxs, ns, dim, self.cache_dim, keys, stream)
+        else:
+            self.BAM_FS.read_feature_merged(len(outs), outs, idxs, ns, dim, self.cache_dim, stream)
+        del keep_alive  # stream-ordered: safe to release once the launch is queued
+
+        return_ten = self.return_torch_buffer.pop(0)
+        return_b = self.window_buffer.pop(0)
+        self.GIDS_time += time.time() - t0
+        cpu_access_count = self.BAM_FS.get_cpu_access_count()
+        self.prev_cpu_access = int(cpu_access_count / num_iter)
+        self.BAM_FS.flush_cpu_access_count()
+        return _with_features(return_b, return_ten)
+
+    # ---------------------------------------------------------------- stats
+    def print_stats(self):
+        """Print and reset timers and cache counters (GIDS.py:1062-1080)."""
+        print("GIDS time: ", self.GIDS_time)
+        print("WB time: ", self.WB_time)
+        self.WB_time = 0.0
+        self.GIDS_time = 0.0
+        self.BAM_FS.print_stats()
+
+    def get_stats(self):
+        """Cumulative cache counters as a dict (extension)."""
+        return self.BAM_FS.get_stats()
+
+    # --------------------------------------------------------- backing store
+    def store_tensor(self, in_ten, offset):
+        """Write rows to the backing store (GIDS.py:1083-1093 -> gids_nvme.cu:616-663)."""
+        t = in_ten.contiguous()
+        self.BAM_FS.store_tensor(t.data_ptr(), len(t), offset)
+
+    def store_mmap_tensor(self, in_ten, offset):
+        """Same from a numpy (memmap) array (GIDS.py:1095-1116)."""
+        import numpy as np
+
+        y = np.ascontiguousarray(in_ten)
+        self.BAM_FS.store_tensor(y.ctypes.data, len(y), offset)
+
+    def read_tensor(self, num, offset):
+        """Print ``num`` elements from element ``offset`` (GIDS.py:1118-1122)."""
+        self.BAM_FS.read_tensor(num, offset)
+
+    def flush_cache(self):
+        """Drop resident pages (GIDS.py:1124-1128)."""
+        self.BAM_FS.flush_cache()
+
+
+# --------------------------------------------------------------------- loader
+class _PrefetchingIter:
+    """Iterator that appends gathered features to each sampled batch (GIDS.py:204-258)."""
+
+    def __init__(self, dataloader, dataloader_it, GIDS_Loader=None):
+        self.dataloader_it = dataloader_it
+        self.dataloader = dataloader
+        self.graph_sampler = getattr(dataloader, "graph_sampler", None)
+        self.GIDS_Loader = GIDS_Loader
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        return self.GIDS_Loader.fetch_feature(self.dataloader.dim, self.dataloader_it, self.GIDS_Loader.gids_device)
+
+
+def GIDS_DGLDataLoader(graph, indices, graph_sampler, batch_size, dim, GIDS, device=None, use_ddp=False,
+                       ddp_seed=0, drop_last=False, shuffle=False, use_alternate_streams=None, **kwargs):
+    """DGL DataLoader whose iterator appends GIDS-gathered features
+    (GIDS.py:262-488). Needs dgl; it is imported here, so the rest of the
+    package works without it."""
+    from ._dgl_loader import make_dgl_loader
+
+    return make_dgl_loader(graph, indices, graph_sampler, batch_size, dim, GIDS, device=device, use_ddp=use_ddp,
+                           ddp_seed=ddp_seed, drop_last=drop_last, shuffle=shuffle,
+                           use_alternate_streams=use_alternate_streams, **kwargs)

@@ -1,0 +1,210 @@
+"""Seeded synthetic graphs and a multi-layer neighbour sampler.
+
+The reference feeds fetch_feature with node ids from DGL's
+MultiLayerNeighborSampler over IGB/OGB graphs (homogenous_train.py:201-203,
+dataloader.py). Neither DGL nor the datasets exist on the build or GPU
+machines, so the benchmarks draw ids from this module instead.
+
+Graph model (CSC, defined by hash functions so that a 100M-node graph needs
+no edge list): every node u has an out-degree weight d_u drawn from a Zipf(alpha)
+law truncated to [1, K], with K chosen so that the mean is ``mean_degree``;
+every node v has Poisson(mean_degree) in-edges whose sources are drawn with
+probability proportional to d_u ("neighbours chosen uniformly" among edge
+ends). Neighbour j of v is a pure function of (seed, v, j), so the graph is
+fixed by its seed; ``materialize`` builds the explicit CSC for small graphs.
+
+Sampler (MultiLayerNeighborSampler semantics): for fanouts [f_0, ..., f_L-1],
+hop h (from the seeds outward) takes min(f_{L-1-h}, in_degree) distinct
+in-edges of every node of the current frontier; the next frontier is the
+current node set plus the new sources in order of first appearance, and the
+last node set is ``input_nodes`` (seeds first).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+_M1 = np.int64(np.uint64(0xBF58476D1CE4E5B9).astype(np.int64))
+_M2 = np.int64(np.uint64(0x94D049BB133111EB).astype(np.int64))
+_G = np.int64(np.uint64(0x9E3779B97F4A7C15).astype(np.int64))
+
+
+def _i64(v: int) -> int:
+    """Python int wrapped to a signed 64-bit value."""
+    v &= (1 << 64) - 1
+    return v - (1 << 64) if v >= (1 << 63) else v
+
+
+def _srl(z: torch.Tensor, k: int) -> torch.Tensor:
+    return (z >> k) & ((1 << (64 - k)) - 1)
+
+
+def _mix(z: torch.Tensor) -> torch.Tensor:
+    z = (z ^ _srl(z, 30)) * int(_M1)
+    z = (z ^ _srl(z, 27)) * int(_M2)
+    return z ^ _srl(z, 31)
+
+
+def _uniform(z: torch.Tensor) -> torch.Tensor:
+    """uniform [0, 1) float64 from 53 hash bits"""
+    return _srl(_mix(z), 11).to(torch.float64) * (2.0 ** -53)
+
+
+def zipf_truncation(alpha: float, mean: float) -> int:
+    """Smallest K with E[d] >= mean for P(d = k) ~ k^-alpha on [1, K]."""
+
+    def m(K):
+        k = np.arange(1, K + 1, dtype=np.float64)
+        w = k ** -alpha
+        return float((k * w).sum() / w.sum())
+
+    if mean <= 1.0:
+        return 1
+    hi = 2
+    while m(hi) < mean:  # the mean grows with K: double, then bisect
+        hi *= 2
+        if hi > (1 << 26):
+            raise ValueError("mean degree not reachable with this alpha")
+    lo = hi // 2
+    while hi - lo > 1:
+        mid = (lo + hi) // 2
+        if m(mid) >= mean:
+            hi = mid
+        else:
+            lo = mid
+    return hi
+
+
+class SyntheticGraph:
+    def __init__(self, num_nodes: int, mean_degree: float = 15.0, alpha: float = 1.1, seed: int = 0,
+                 device="cpu"):
+        self.N = int(num_nodes)
+        self.mean = float(mean_degree)
+        self.alpha = float(alpha)
+        self.seed = int(seed)
+        self.device = torch.device(device)
+        self.K = zipf_truncation(self.alpha, self.mean)
+        k = np.arange(1, self.K + 1, dtype=np.float64)
+        w = k ** -self.alpha
+        self._deg_cdf = torch.tensor(np.cumsum(w / w.sum()), dtype=torch.float64, device=self.device)
+        # Poisson(mean) in-degree table, capped where the tail is below 1e-12
+        kmax = int(self.mean + 12 * math.sqrt(self.mean) + 20)
+        pmf = [math.exp(-self.mean)]
+        for i in range(1, kmax + 1):
+            pmf.append(pmf[-1] * self.mean / i)
+        self.max_in_degree = kmax
+        self._in_cdf = torch.tensor(np.cumsum(pmf) / np.sum(pmf), dtype=torch.float64, device=self.device)
+        # out-degree class of every node, nodes grouped by class
+        d = self.out_degree(torch.arange(self.N, device=self.device))
+        self._order = torch.argsort(d, stable=True)
+        counts = torch.bincount(d - 1, minlength=self.K)
+        self._class_count = counts
+        self._class_off = torch.cumsum(counts, 0) - counts
+        mass = counts.to(torch.float64) * torch.arange(1, self.K + 1, device=self.device, dtype=torch.float64)
+        self._class_cdf = torch.cumsum(mass / mass.sum(), 0)
+        del d
+
+    def _h(self, salt: int, x: torch.Tensor) -> torch.Tensor:
+        return x * int(_G) + _i64((self.seed * 1_000_003 + salt) * int(_M1))
+
+    def out_degree(self, u: torch.Tensor) -> torch.Tensor:
+        x = _uniform(self._h(1, u))
+        return torch.searchsorted(self._deg_cdf, x, right=True).clamp_(max=self.K - 1) + 1
+
+    def in_degree(self, v: torch.Tensor) -> torch.Tensor:
+        x = _uniform(self._h(2, v))
+        return torch.searchsorted(self._in_cdf, x, right=True).clamp_(max=self.max_in_degree)
+
+    def in_neighbor(self, v: torch.Tensor, j: torch.Tensor) -> torch.Tensor:
+        """Source of in-edge j of v (j < in_degree(v))."""
+        e = v * (self.max_in_degree + 1) + j
+        c = torch.searchsorted(self._class_cdf, _uniform(self._h(3, e)), right=True).clamp_(max=self.K - 1)
+        cnt = self._class_count[c]
+        off = (_uniform(self._h(4, e)) * cnt.to(torch.float64)).to(torch.int64).clamp_(min=0)
+        off = torch.minimum(off, (cnt - 1).clamp(min=0))
+        return self._order[self._class_off[c] + off]
+
+    def materialize(self):
+        """Explicit CSC (indptr, indices) of the graph (small graphs only)."""
+        v = torch.arange(self.N, device=self.device)
+        deg = self.in_degree(v)
+        indptr = torch.zeros(self.N + 1, dtype=torch.int64, device=self.device)
+        indptr[1:] = torch.cumsum(deg, 0)
+        rows = torch.repeat_interleave(v, deg)
+        j = torch.arange(int(indptr[-1]), device=self.device) - indptr[:-1].repeat_interleave(deg)
+        return indptr, self.in_neighbor(rows, j)
+
+
+def unique_first(x: torch.Tensor) -> torch.Tensor:
+    """Unique values of x in order of first appearance."""
+    if x.numel() == 0:
+        return x
+    u, inv = torch.unique(x, return_inverse=True)
+    first = torch.full((u.numel(),), x.numel(), dtype=torch.int64, device=x.device)
+    first.scatter_reduce_(0, inv, torch.arange(x.numel(), device=x.device), reduce="amin")
+    return u[torch.argsort(first)]
+
+
+class NeighborSampler:
+    """Seeded stand-in for dgl.dataloading.MultiLayerNeighborSampler(fanouts)."""
+
+    def __init__(self, graph: SyntheticGraph, fanouts, seed: int = 1000):
+        self.g = graph
+        self.fanouts = [int(f) for f in fanouts]
+        self.gen = torch.Generator(device=graph.device)
+        self.gen.manual_seed(int(seed))
+
+    def sample_neighbors(self, frontier: torch.Tensor, fanout: int):
+        """(dst, src) pairs: min(fanout, deg) distinct in-edges per frontier node."""
+        g = self.g
+        deg = g.in_degree(frontier)
+        if frontier.numel() == 0:
+            return frontier, frontier
+        D = int(deg.max().item())
+        if D == 0:
+            e = frontier[:0]
+            return e, e
+        keys = torch.rand((frontier.numel(), D), generator=self.gen, device=frontier.device)
+        pos = torch.arange(D, device=frontier.device)
+        keys.masked_fill_(pos[None, :] >= deg[:, None], 2.0)
+        take = min(fanout, D)
+        j = torch.topk(keys, take, dim=1, largest=False).indices
+        valid = torch.arange(take, device=frontier.device)[None, :] < torch.clamp(deg, max=fanout)[:, None]
+        dst = frontier[:, None].expand(-1, take)[valid]
+        jj = j[valid]
+        return dst, g.in_neighbor(dst, jj)
+
+    def sample(self, seeds: torch.Tensor):
+        """input_nodes (seeds first, then new sources by first appearance), seeds."""
+        nodes = unique_first(seeds.to(self.g.device))
+        for f in reversed(self.fanouts):
+            _, src = self.sample_neighbors(nodes, f)
+            new = unique_first(src)
+            new = new[~torch.isin(new, nodes)]
+            nodes = torch.cat([nodes, new])
+        return nodes, seeds
+
+
+def seed_batches(num_nodes: int, batch_size: int, n_batches: int, seed: int, device="cpu", zipf_alpha=None):
+    """Seed-node batches: uniform over [0, N) or, with zipf_alpha, Zipf over node ids."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed))
+    out = []
+    for _ in range(n_batches):
+        if zipf_alpha is None:
+            s = torch.randint(0, num_nodes, (batch_size * 2,), generator=gen, device=device)
+        else:
+            # inverse-CDF sampling of a Zipf law over ranks 1..N, ranks scattered over ids
+            u = torch.rand(batch_size * 2, generator=gen, device=device, dtype=torch.float64)
+            a = float(zipf_alpha)
+            if abs(a - 1.0) < 1e-9:
+                r = torch.exp(u * math.log(num_nodes))
+            else:
+                r = (1 + u * (num_nodes ** (1 - a) - 1)) ** (1 / (1 - a))
+            rank = r.to(torch.int64).clamp_(0, num_nodes - 1)
+            s = _srl(_mix(rank * int(_G) + 77), 1) % num_nodes
+        s = unique_first(s)[:batch_size]
+        out.append(s)
+    return out

@@ -1,0 +1,289 @@
+// pybind11 module BAM_Feature_Store: the reference's Python boundary
+// (gids_module/gids_nvme.cu:823-893) rebuilt over the C ABI of libgids_b200.
+// Class and method names, argument order and meaning follow the reference;
+// every method releases the GIL and raises RuntimeError on failure. Methods
+// marked "extension" have no reference counterpart.
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gids_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+void check(int rc) {
+  if (rc != GIDS_OK) {
+    char buf[1024];
+    gids_last_error(buf, sizeof(buf));
+    throw std::runtime_error(std::string("gids: ") + gids_strerror(rc) + ": " + buf);
+  }
+}
+
+struct Controllers {
+  gids_ctrls_t* c = nullptr;
+  uint32_t n_ctrls = 0;
+  Controllers() { check(gids_ctrls_create(&c)); }
+  ~Controllers() {
+    if (c) gids_ctrls_destroy(c);
+  }
+  Controllers(const Controllers&) = delete;
+  // GIDS_Controllers::init_GIDS_controllers (gids_nvme.cu:93-107)
+  void init(uint32_t n, uint64_t q_depth, uint64_t n_queues, const std::vector<int>& ssd_list) {
+    std::vector<int32_t> l(ssd_list.begin(), ssd_list.end());
+    if (l.size() < n) throw std::runtime_error("ssd_list shorter than the number of controllers");
+    check(gids_ctrls_init(c, n, q_depth, n_queues, l.data()));
+    n_ctrls = n;
+  }
+  // extension: emulated-SSD capacity (bytes per SSD, 0 = whole stripe) and file pattern
+  void set_emulation(uint64_t capacity, const std::string& pattern) {
+    check(gids_ctrls_set_emulation(c, capacity, pattern.c_str()));
+  }
+};
+
+class FeatureStore {
+ public:
+  explicit FeatureStore(uint32_t eb) : eb_(eb) {}
+  ~FeatureStore() {
+    if (s_) gids_store_destroy(s_);
+  }
+  FeatureStore(const FeatureStore&) = delete;
+
+  gids_store_t* s() const {
+    if (!s_) throw std::runtime_error("gids: init_controllers has not been called");
+    return s_;
+  }
+  // extension: device for the store (default: the current CUDA device at init_controllers)
+  void set_device(int d) {
+    if (s_) throw std::runtime_error("gids: set_device after init_controllers");
+    device_ = d;
+  }
+  // BAM_Feature_Store<T>::init_controllers (gids_nvme.cu:166-221)
+  void init_controllers(Controllers& ctrl, uint32_t ps, uint64_t read_off, uint64_t cache_size, uint64_t num_ele,
+                        uint64_t num_ssd) {
+    if (s_) throw std::runtime_error("gids: init_controllers called twice");
+    int dev = device_;
+    if (dev < 0) check(gids_current_device(&dev));
+    gids_store_t* s = nullptr;
+    check(gids_store_create(&s, eb_, dev));
+    int rc = gids_store_init_controllers(s, ctrl.c, ps, read_off, cache_size, num_ele, num_ssd);
+    if (rc != GIDS_OK) {
+      char buf[1024];
+      gids_last_error(buf, sizeof(buf));
+      gids_store_destroy(s);
+      throw std::runtime_error(std::string("gids: ") + gids_strerror(rc) + ": " + buf);
+    }
+    s_ = s;
+    page_size_ = ps;
+  }
+  // read_feature (gids_nvme.cu:324-364)
+  void read_feature(uint64_t out, uint64_t idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
+                    uint64_t stream) {
+    check(gids_read_feature(s(), (void*)out, (const int64_t*)idx, n, dim, cache_dim, key_off, (void*)stream));
+  }
+  // read_feature_hetero / read_feature_merged_hetero (gids_nvme.cu:382-445, 531-593)
+  void read_hetero(int k, const std::vector<uint64_t>& outs, const std::vector<uint64_t>& idxs,
+                   const std::vector<uint64_t>& ns, int dim, int cache_dim, const std::vector<uint64_t>& key_off,
+                   uint64_t stream) {
+    check_lists(k, outs, idxs, ns);
+    if (key_off.size() < (size_t)k) throw std::runtime_error("gids: key_off list shorter than k");
+    check(gids_read_feature_multi(s(), k, (void* const*)outs.data(), (const int64_t* const*)idxs.data(), ns.data(),
+                                  dim, cache_dim, key_off.data(), (void*)stream));
+  }
+  // read_feature_merged (gids_nvme.cu:456-518)
+  void read_merged(int k, const std::vector<uint64_t>& outs, const std::vector<uint64_t>& idxs,
+                   const std::vector<uint64_t>& ns, int dim, int cache_dim, uint64_t stream) {
+    check_lists(k, outs, idxs, ns);
+    check(gids_read_feature_multi(s(), k, (void* const*)outs.data(), (const int64_t* const*)idxs.data(), ns.data(),
+                                  dim, cache_dim, nullptr, (void*)stream));
+  }
+  // set_window_buffering (gids_nvme.cu:242-249)
+  void set_window_buffering(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
+    check(gids_set_window_buffering(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
+  }
+  // cpu_backing_buffer (gids_nvme.cu:123-139)
+  void cpu_backing_buffer(uint64_t dim, uint64_t len) { check(gids_cpu_backing_buffer(s(), dim, len)); }
+  // set_cpu_buffer (gids_nvme.cu:694-711)
+  void set_cpu_buffer(uint64_t idx, int num) { check(gids_set_cpu_buffer(s(), (const int64_t*)idx, num)); }
+  // flush_cache (gids_nvme.cu:673-677)
+  void flush_cache() { check(gids_flush_cache(s())); }
+  // store_tensor (gids_nvme.cu:616-663)
+  void store_tensor(uint64_t ptr, uint64_t num, uint64_t offset) {
+    check(gids_store_tensor(s(), (const void*)ptr, num, offset));
+  }
+  // read_tensor (gids_nvme.cu:764-770): prints num elements from element offset
+  void read_tensor(uint64_t num, uint64_t offset) {
+    std::vector<char> buf(num * eb_);
+    check(gids_read_range_host(s(), buf.data(), buf.size(), offset * eb_));
+    printf("offset:%llu\n", (unsigned long long)offset);
+    for (uint64_t i = 0; i < num; i++) {
+      if (eb_ == 4) {
+        float v;
+        memcpy(&v, buf.data() + i * 4, 4);
+        printf("read data: %f\n", v);
+      } else if (eb_ == 8) {
+        long long v;
+        memcpy(&v, buf.data() + i * 8, 8);
+        printf("read data: %lld\n", v);
+      } else {
+        uint16_t v;
+        memcpy(&v, buf.data() + i * 2, 2);
+        printf("read data: 0x%04x\n", v);
+      }
+    }
+    fflush(stdout);
+  }
+  // get_cpu_access_count / flush_cpu_access_count (gids_nvme.cu:779-794)
+  uint32_t get_cpu_access_count() {
+    uint32_t v = 0;
+    check(gids_get_cpu_access_count(s(), &v));
+    return v;
+  }
+  void flush_cpu_access_count() { check(gids_flush_cpu_access_count(s())); }
+  // print_stats (gids_nvme.cu:279-300)
+  void print_stats() { check(gids_print_stats(s())); }
+  // set_offsets / get_offset_array (gids_nvme.cu:721-748): host triple used by
+  // the graph-on-SSD sampler, kept for interface compatibility
+  void set_offsets(uint64_t a, uint64_t b, uint64_t c) { offsets_ = {a, b, c}; }
+  uint64_t get_offset_array() { return (uint64_t)(uintptr_t)offsets_.data(); }
+
+  // ---- extensions
+  void set_synchronous(bool v) { check(gids_store_set_synchronous(s(), v ? 1 : 0)); }
+  void set_row_layout(uint32_t cache_dim) { check(gids_store_set_row_layout(s(), cache_dim)); }
+  void synchronize() { check(gids_store_synchronize(s())); }
+  py::dict get_stats() {
+    uint64_t v[GIDS_STAT_COUNT] = {0};
+    {
+      py::gil_scoped_release r;
+      check(gids_get_stats(s(), v, GIDS_STAT_COUNT));
+    }
+    py::dict d;
+    static const char* names[] = {"access",      "hit",       "miss",          "read_io",     "bypass",
+                                  "cpu_rows",    "rows",      "wait_timeouts", "bad_ids",     "bytes_hit",
+                                  "bytes_miss",  "bytes_bypass", "bytes_cpu",   "evictions",   "launches"};
+    for (int i = 0; i < 15; i++) d[names[i]] = v[i];
+    return d;
+  }
+  void reset_stats() { check(gids_reset_stats(s())); }
+  double kernel_time_ms() {
+    double v = 0;
+    check(gids_get_kernel_time_ms(s(), &v));
+    return v;
+  }
+  void fill_synthetic(int kind, uint64_t seed, int threads) { check(gids_fill_synthetic(s(), kind, seed, threads)); }
+  void write_range(uint64_t ptr, uint64_t nbytes, uint64_t offset) {
+    check(gids_write_range(s(), (const void*)ptr, nbytes, offset));
+  }
+  void read_range_into(uint64_t dst, uint64_t nbytes, uint64_t offset) {
+    check(gids_read_range_host(s(), (void*)dst, nbytes, offset));
+  }
+  py::dict geometry() {
+    uint64_t g[6] = {0};
+    check(gids_store_geometry(s(), g, 6));
+    py::dict d;
+    d["range_pages"] = g[0];
+    d["wrap_pages"] = g[1];
+    d["ssd_bytes"] = g[2];
+    d["cache_slots"] = g[3];
+    d["page_size"] = g[4];
+    d["num_ssd"] = g[5];
+    return d;
+  }
+  uint32_t elem_bytes() const { return eb_; }
+  uint64_t handle() const { return (uint64_t)(uintptr_t)s(); }
+
+ private:
+  static void check_lists(int k, const std::vector<uint64_t>& o, const std::vector<uint64_t>& i,
+                          const std::vector<uint64_t>& n) {
+    if (k < 0 || o.size() < (size_t)k || i.size() < (size_t)k || n.size() < (size_t)k)
+      throw std::runtime_error("gids: pointer lists shorter than k");
+  }
+  uint32_t eb_;
+  int device_ = -1;
+  uint32_t page_size_ = 0;
+  gids_store_t* s_ = nullptr;
+  std::vector<uint64_t> offsets_{0, 0, 0};
+};
+
+template <uint32_t EB, int TAG>
+struct TypedStore : FeatureStore {
+  TypedStore() : FeatureStore(EB) {}
+};
+
+template <uint32_t EB, int TAG>
+void bind_store(py::module_& m, const char* name) {
+  using S = TypedStore<EB, TAG>;
+  using R = py::call_guard<py::gil_scoped_release>;
+  py::class_<S>(m, name)
+      .def(py::init<>())
+      .def("init_controllers", &S::init_controllers, py::arg("ctrl"), py::arg("ps"), py::arg("read_off"),
+           py::arg("cache_size"), py::arg("num_ele"), py::arg("num_ssd") = 1, R())
+      .def("read_feature", &S::read_feature, py::arg("i_ptr"), py::arg("i_index_ptr"), py::arg("num_index"),
+           py::arg("dim"), py::arg("cache_dim"), py::arg("key_off") = 0, py::arg("stream") = 0, R())
+      .def("read_feature_hetero", &S::read_hetero, py::arg("num_iter"), py::arg("i_ptr_list"),
+           py::arg("i_index_ptr_list"), py::arg("num_index"), py::arg("dim"), py::arg("cache_dim"),
+           py::arg("key_off"), py::arg("stream") = 0, R())
+      .def("read_feature_merged_hetero", &S::read_hetero, py::arg("num_iter"), py::arg("i_ptr_list"),
+           py::arg("i_index_ptr_list"), py::arg("num_index"), py::arg("dim"), py::arg("cache_dim"),
+           py::arg("key_off"), py::arg("stream") = 0, R())
+      .def("read_feature_merged", &S::read_merged, py::arg("num_iter"), py::arg("i_ptr_list"),
+           py::arg("i_index_ptr_list"), py::arg("num_index"), py::arg("dim"), py::arg("cache_dim") = 1024,
+           py::arg("stream") = 0, R())
+      .def("set_window_buffering", &S::set_window_buffering, py::arg("id_idx"), py::arg("num_pages"),
+           py::arg("hash_off") = 0, py::arg("stream") = 0, R())
+      .def("cpu_backing_buffer", &S::cpu_backing_buffer, py::arg("dim"), py::arg("len"), R())
+      .def("set_cpu_buffer", &S::set_cpu_buffer, py::arg("idx_buffer"), py::arg("num"), R())
+      .def("flush_cache", &S::flush_cache, R())
+      .def("store_tensor", &S::store_tensor, py::arg("tensor_ptr"), py::arg("num"), py::arg("offset"), R())
+      .def("read_tensor", &S::read_tensor, py::arg("num"), py::arg("offset"), R())
+      .def("get_array_ptr",
+           [](S&) -> uint64_t {
+             throw std::runtime_error(
+                 "gids: get_array_ptr exposes the BaM device array used by graph-structure sampling, "
+                 "which this library does not implement");
+           })
+      .def("get_offset_array", &S::get_offset_array)
+      .def("set_offsets", &S::set_offsets)
+      .def("get_cpu_access_count", &S::get_cpu_access_count, R())
+      .def("flush_cpu_access_count", &S::flush_cpu_access_count, R())
+      .def("print_stats", &S::print_stats, R())
+      // extensions
+      .def("set_device", &S::set_device)
+      .def("set_synchronous", &S::set_synchronous, R())
+      .def("set_row_layout", &S::set_row_layout, R())
+      .def("synchronize", &S::synchronize, R())
+      .def("get_stats", &S::get_stats)
+      .def("reset_stats", &S::reset_stats, R())
+      .def("kernel_time_ms", &S::kernel_time_ms, R())
+      .def("fill_synthetic", &S::fill_synthetic, py::arg("kind"), py::arg("seed"), py::arg("threads") = 0, R())
+      .def("write_range", &S::write_range, R())
+      .def("read_range_into", &S::read_range_into, R())
+      .def("geometry", &S::geometry)
+      .def_property_readonly("elem_bytes", &S::elem_bytes)
+      .def_property_readonly("handle", &S::handle);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(BAM_Feature_Store, m) {
+  m.doc() = "B200 GIDS feature store (drop-in for the reference's BAM_Feature_Store pybind module)";
+  py::class_<Controllers>(m, "GIDS_Controllers")
+      .def(py::init<>())
+      .def("init_GIDS_controllers", &Controllers::init, py::arg("num_ctrls"), py::arg("q_depth"), py::arg("num_q"),
+           py::arg("ssd_list"))
+      .def("set_emulation", &Controllers::set_emulation, py::arg("capacity_bytes_per_ssd") = 0,
+           py::arg("path_pattern") = std::string())
+      .def_readonly("n_ctrls", &Controllers::n_ctrls);
+  bind_store<4, 0>(m, "BAM_Feature_Store_float");
+  bind_store<8, 0>(m, "BAM_Feature_Store_long");
+  bind_store<2, 0>(m, "BAM_Feature_Store_half");
+  bind_store<2, 1>(m, "BAM_Feature_Store_bfloat16");
+  m.def("version", []() { return std::string(gids_version()); });
+}

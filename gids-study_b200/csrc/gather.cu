@@ -1,0 +1,493 @@
+// Feature-gather kernels for sm_100a.
+//
+// One kernel serves every read entry point of the reference's
+// BAM_Feature_Store (read_feature, read_feature_hetero, read_feature_merged,
+// read_feature_merged_hetero; gids_nvme.cu:324-593) and both of its kernels
+// (read_feature_kernel and read_feature_kernel_with_cpu_backing_memory,
+// gids_kernel.cu:60-175):
+//
+//   out_t[i, 0:dim] = range[(idx_t[i] + key_off_t) * cache_dim + (0:dim)]
+//
+// Work is split into chunks of 32 lanes. A chunk covers 32 >> seg_shift rows
+// and each row gets (1 << seg_shift) lanes, one per page the row can touch,
+// so the lookups of a whole chunk run in parallel instead of one dependent
+// chain per row. Per chunk a warp:
+//   1. loads the node ids, checks them against the range, and looks rows up in
+//      the constant CPU buffer (bitmap + rank, in L2);
+//   2. deduplicates page references inside the warp (__match_any_sync, the
+//      reference's coalesce_page, page_cache_backup.h:1514-1550) and lets one
+//      leader per page take `count` references on the page-table word;
+//   3. fills the pages it won (BUSY) from the emulated SSDs after a warp-wide
+//      clock sweep for victim slots (32 candidates per atomic on the hand),
+//      and publishes them VALID;
+//   4. waits, with a bound, for pages another warp is filling; a wait that
+//      runs out, or a fill that found no slot, reads the page straight from
+//      the backing store (always correct: the store is read-only here);
+//   5. copies all segments of the chunk with 16-byte vector loads/stores,
+//      eight vectors in flight per lane, and drops its page references.
+// The state-word protocol follows range_d_t::acquire_page/release_page
+// (page_cache_backup.h:1278-1403, 1166-1229) with a 64-bit word that also
+// holds the slot; eviction follows find_slot (:2107-2256) with a reference
+// bit per slot (second chance) and every spin bounded.
+#include <cuda_runtime.h>
+
+#include "gids_internal.hpp"
+
+namespace gids {
+namespace {
+
+// ------------------------------------------------------------ atomics (gpu scope)
+__device__ __forceinline__ unsigned long long atom_add_acquire(unsigned long long* p, unsigned long long v) {
+  unsigned long long r;
+  asm volatile("atom.acquire.gpu.global.add.u64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  return r;
+}
+__device__ __forceinline__ unsigned long long atom_or_acquire(unsigned long long* p, unsigned long long v) {
+  unsigned long long r;
+  asm volatile("atom.acquire.gpu.global.or.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  return r;
+}
+__device__ __forceinline__ unsigned long long atom_and_relaxed(unsigned long long* p, unsigned long long v) {
+  unsigned long long r;
+  asm volatile("atom.relaxed.gpu.global.and.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  return r;
+}
+__device__ __forceinline__ void red_add_release(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long atom_cas_acq_rel(unsigned long long* p, unsigned long long cmp,
+                                                               unsigned long long val) {
+  unsigned long long r;
+  asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;" : "=l"(r) : "l"(p), "l"(cmp), "l"(val) : "memory");
+  return r;
+}
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+  unsigned long long r;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  return r;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
+  unsigned long long r;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  return r;
+}
+
+// ------------------------------------------------------------ vector copies
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<16> {
+  using T = int4;
+};
+template <>
+struct VecT<8> {
+  using T = int2;
+};
+template <>
+struct VecT<4> {
+  using T = int;
+};
+template <>
+struct VecT<2> {
+  using T = short;
+};
+
+struct SegDesc {
+  const char* src;  // nullptr: write zeros
+  char* dst;
+  uint32_t len;
+  uint32_t pad;
+};
+
+constexpr int WARPS = GATHER_THREADS / 32;
+constexpr int INFLIGHT = 8;  // vectors in flight per lane
+
+// Copies the first nseg segments of sd with the whole warp. Control flow is
+// warp-uniform: every lane walks the same (segment, block) cursor.
+template <int VEC>
+__device__ __forceinline__ void copy_segments(const SegDesc* sd, int nseg, int lane) {
+  using V = typename VecT<VEC>::T;
+  int j = 0;
+  uint32_t m = 0;
+  while (j < nseg) {
+    V v[INFLIGHT];
+    char* dp[INFLIGHT];
+#pragma unroll
+    for (int q = 0; q < INFLIGHT; q++) {
+      dp[q] = nullptr;
+      if (j < nseg) {
+        const uint32_t len = sd[j].len;
+        const uint32_t off = (m * 32u + (uint32_t)lane) * VEC;
+        if (off < len) {
+          const char* s = sd[j].src;
+          dp[q] = sd[j].dst + off;
+          if (s)
+            v[q] = __ldcg(reinterpret_cast<const V*>(s + off));
+          else
+            v[q] = V{};
+        }
+        m++;
+        if (m * 32u * VEC >= len) {
+          m = 0;
+          j++;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < INFLIGHT; q++)
+      if (dp[q]) __stcs(reinterpret_cast<V*>(dp[q]), v[q]);
+  }
+}
+
+// Whole-page copy from the backing store into a cache slot (16-byte vectors;
+// pages are >= 512 B, power-of-two sized, and page-aligned on both sides).
+__device__ __forceinline__ void copy_page(const char* __restrict__ src, char* __restrict__ dst, uint32_t page_size,
+                                          int lane) {
+  for (uint32_t base = 0; base < page_size; base += 32u * 16u * INFLIGHT) {
+    int4 v[INFLIGHT];
+#pragma unroll
+    for (int q = 0; q < INFLIGHT; q++) {
+      const uint32_t off = base + ((uint32_t)q * 32u + (uint32_t)lane) * 16u;
+      if (off < page_size) v[q] = __ldcg(reinterpret_cast<const int4*>(src + off));
+    }
+#pragma unroll
+    for (int q = 0; q < INFLIGHT; q++) {
+      const uint32_t off = base + ((uint32_t)q * 32u + (uint32_t)lane) * 16u;
+      if (off < page_size) __stcg(reinterpret_cast<int4*>(dst + off), v[q]);
+    }
+  }
+}
+
+// Address of logical page p on the emulated SSDs (page_cache_backup.h:626-652,
+// STRIPE): SSD p % n, device page page_start + p / n, after the wrap.
+__device__ __forceinline__ const char* backing_addr(const DevBacking& b, uint64_t p, uint32_t shift) {
+  const uint64_t q = p % b.wrap_pages;
+  const uint32_t c = (uint32_t)(q % b.n_ssd);
+  const uint64_t dp = b.page_start + q / b.n_ssd;
+  return b.ssd[c] + (dp << shift);
+}
+
+// Saturating decrement of a window-buffer pin counter (bounded CAS loop).
+__device__ __forceinline__ void wb_consume(unsigned int* w, unsigned int cnt) {
+  unsigned int v = *reinterpret_cast<volatile unsigned int*>(w);
+  for (int it = 0; v != 0 && it < 64; it++) {
+    const unsigned int nv = v > cnt ? v - cnt : 0u;
+    const unsigned int r = atomicCAS(w, v, nv);
+    if (r == v) break;
+    v = r;
+  }
+}
+
+enum { K_ROWS, K_CPU, K_BAD, K_ACCESS, K_HIT, K_MISS, K_BYPASS, K_READIO, K_TIMEOUT, K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_N };
+__constant__ int kStatMap[K_N] = {GIDS_STAT_ROWS,       GIDS_STAT_CPU_ROWS,   GIDS_STAT_BAD_IDS,    GIDS_STAT_ACCESS,
+                                  GIDS_STAT_HIT,        GIDS_STAT_MISS,       GIDS_STAT_BYPASS,     GIDS_STAT_READ_IO,
+                                  GIDS_STAT_WAIT_TIMEOUT, GIDS_STAT_BYTES_HIT, GIDS_STAT_BYTES_MISS, GIDS_STAT_BYTES_BYPASS,
+                                  GIDS_STAT_BYTES_CPU,  GIDS_STAT_EVICTIONS};
+
+template <int VEC>
+__global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_constant__ GatherArgs a) {
+  __shared__ SegDesc seg_sh[WARPS][32];
+  __shared__ unsigned long long cnt_sh[WARPS][K_N];  // warp-private counters
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  SegDesc* sd = seg_sh[wib];
+  unsigned long long* acc = cnt_sh[wib];
+  if (lane < K_N) acc[lane] = 0;
+  __syncwarp();
+  const uint32_t seg_shift = a.seg_shift;
+  const uint32_t seg_mask = (1u << seg_shift) - 1u;
+  const uint32_t rpc = 32u >> seg_shift;
+  const uint32_t shift = a.c.page_shift;
+  const uint64_t psize = a.c.page_size;
+  const bool have_cache = a.c.n_slots != 0;
+  const uint64_t n_warps = (uint64_t)gridDim.x * WARPS;
+
+  int ti = 0;
+  for (uint64_t chunk = (uint64_t)blockIdx.x * WARPS + wib; chunk < a.total_chunks; chunk += n_warps) {
+    while (ti + 1 < a.k && a.t[ti + 1].chunk_begin <= chunk) ti++;
+    const GatherTuple& T = a.t[ti];
+    const uint64_t row = (chunk - T.chunk_begin) * rpc + ((uint32_t)lane >> seg_shift);
+    const uint32_t sidx = (uint32_t)lane & seg_mask;
+    const bool row_ok = row < T.n;
+
+    // ---- 1. node id, range check, constant CPU buffer lookup
+    int64_t id = row_ok ? __ldg(T.idx + row) : 0;
+    const uint64_t r = (uint64_t)id + T.key_off;
+    const bool bad = row_ok && (id < 0 || r >= a.n_rows);
+    const bool live = row_ok && !bad;
+    bool pinned = false;
+    uint64_t cpu_slot = 0;
+    if (live && a.cpu.mode == 1) {
+      pinned = r < a.cpu.seq_len;
+      cpu_slot = r;
+    } else if (live && a.cpu.mode == 2) {
+      const uint64_t w = r >> 6;
+      if (w < a.cpu.nwords) {
+        const unsigned long long bits = __ldg(a.cpu.bits + w);
+        const unsigned long long below = bits & ((1ull << (r & 63)) - 1ull);
+        if ((bits >> (r & 63)) & 1ull) {
+          pinned = true;
+          cpu_slot = (uint64_t)__ldg(a.cpu.rank + w) + (uint64_t)__popcll(below);
+        }
+      }
+    }
+
+    // ---- page segment of this lane
+    const uint64_t b0 = r * a.src_stride;
+    const uint64_t p_first = b0 >> shift;
+    const uint64_t p_last = (b0 + a.row_bytes - 1) >> shift;
+    const uint64_t p = p_first + sidx;
+    const bool seg_ok = live && !pinned && p <= p_last;
+    uint32_t s0 = 0, s1 = 0;
+    if (seg_ok) {
+      const uint64_t pb = p << shift;
+      s0 = (uint32_t)((pb > b0 ? pb : b0) - b0);
+      const uint64_t pe = pb + psize, re = b0 + a.row_bytes;
+      s1 = (uint32_t)((pe < re ? pe : re) - b0);
+    }
+
+    // ---- 2. warp dedup + acquire (one leader per distinct page)
+    const unsigned long long key = seg_ok ? (unsigned long long)p : (~0ull - (unsigned long long)lane);
+    const unsigned eq = __match_any_sync(0xffffffffu, key);
+    const int leader = __ffs(eq) - 1;
+    const bool is_leader = seg_ok && leader == lane;
+    const unsigned cnt = __popc(eq);
+    int cls = CLS_NONE;
+    uint64_t slot = 0;
+    unsigned long long* stw = a.c.state + (seg_ok ? p : 0);
+    const bool took_ref = is_leader && have_cache;
+    if (is_leader) {
+      if (!have_cache) {
+        cls = CLS_BYPASS;
+      } else {
+        const unsigned long long old = atom_add_acquire(stw, cnt);
+        if (old & ST_VALID) {
+          cls = CLS_HIT;
+          slot = old >> ST_SLOT_SHIFT;
+        } else if (old & ST_BUSY) {
+          cls = CLS_WAIT;
+        } else {
+          const unsigned long long prev = atom_or_acquire(stw, ST_BUSY);
+          if (prev & ST_VALID) {
+            cls = CLS_HIT;
+            slot = prev >> ST_SLOT_SHIFT;
+          } else if (prev & ST_BUSY) {
+            cls = CLS_WAIT;
+          } else {
+            cls = CLS_OWN;
+          }
+        }
+      }
+    }
+
+    // ---- 3. fills: warp-cooperative clock sweep for victim slots, then copies
+    unsigned pending = __ballot_sync(0xffffffffu, cls == CLS_OWN);
+    if (pending) {
+      for (uint32_t round = 0; pending && round < a.sweep_limit; round++) {
+        unsigned long long base = 0;
+        if (lane == 0) base = atomicAdd(a.c.clock, 32ull);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const uint64_t s = (base + (uint64_t)lane) % a.c.n_slots;
+        const unsigned long long q = ld_relaxed(a.c.slot_page + s);
+        bool cand = false;
+        unsigned long long expect = 0;
+        if (q == SLOT_EMPTY) {
+          cand = true;
+        } else if (a.c.slot_ref[s]) {
+          a.c.slot_ref[s] = 0;  // second chance
+        } else {
+          const unsigned long long st = ld_relaxed(a.c.state + q);
+          if (st == (((unsigned long long)s << ST_SLOT_SHIFT) | ST_VALID) && (!a.c.wb || a.c.wb[q] == 0)) {
+            cand = true;
+            expect = st;
+          }
+        }
+        unsigned cmask = __ballot_sync(0xffffffffu, cand);
+        while (cmask && pending) {
+          const int c = __ffs(cmask) - 1;
+          cmask &= cmask - 1;
+          const int o = __ffs(pending) - 1;
+          const unsigned long long newp = __shfl_sync(0xffffffffu, (unsigned long long)p, o);
+          int ok = 0;
+          if (lane == c) {
+            if (q == SLOT_EMPTY) {
+              ok = atom_cas_acq_rel(a.c.slot_page + s, SLOT_EMPTY, newp) == SLOT_EMPTY;
+            } else if (atom_cas_acq_rel(a.c.state + q, expect, 0ull) == expect) {
+              atomicExch(a.c.slot_page + s, newp);
+              atomicAdd(acc + K_EVICT, 1ull);
+              ok = 1;
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, c);
+          if (ok) {
+            const unsigned long long sl = __shfl_sync(0xffffffffu, (unsigned long long)s, c);
+            if (lane == o) slot = sl;
+            pending &= ~(1u << o);
+          }
+        }
+      }
+      // owners without a slot give the fill up and read the backing store
+      if ((pending >> lane) & 1u) {
+        atom_and_relaxed(stw, ~ST_BUSY);
+        cls = CLS_BYPASS;
+      }
+      unsigned fills = __ballot_sync(0xffffffffu, cls == CLS_OWN);
+      while (fills) {
+        const int o = __ffs(fills) - 1;
+        fills &= fills - 1;
+        const unsigned long long po = __shfl_sync(0xffffffffu, (unsigned long long)p, o);
+        const unsigned long long so = __shfl_sync(0xffffffffu, (unsigned long long)slot, o);
+        copy_page(backing_addr(a.b, po, shift), a.c.slots + (so << shift), a.c.page_size, lane);
+        __syncwarp();
+        if (lane == o) {
+          __threadfence();
+          red_add_release(stw, (so << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
+          acc[K_READIO]++;  // only lane o touches it here
+        }
+      }
+    }
+
+    // ---- 4. bounded wait for pages filled by other warps
+    if (__any_sync(0xffffffffu, cls == CLS_WAIT)) {
+      unsigned ns = 32;
+      for (uint32_t it = 0;; it++) {
+        if (cls == CLS_WAIT) {
+          const unsigned long long v = ld_acquire(stw);
+          if (v & ST_VALID) {
+            cls = CLS_WAITED;
+            slot = v >> ST_SLOT_SHIFT;
+          } else if (!(v & ST_BUSY)) {
+            cls = CLS_BYPASS;  // the filler gave up
+          }
+        }
+        if (!__any_sync(0xffffffffu, cls == CLS_WAIT) || it + 1 >= a.spin_limit) break;
+        __nanosleep(ns);
+        if (ns < 2048) ns <<= 1;
+      }
+      if (cls == CLS_WAIT) {
+        cls = CLS_BYPASS;
+        atomicAdd(acc + K_TIMEOUT, 1ull);
+      }
+    }
+
+    // ---- 5. segment table and copy
+    const int gcls = __shfl_sync(0xffffffffu, cls, leader);
+    const unsigned long long gslot = __shfl_sync(0xffffffffu, (unsigned long long)slot, leader);
+    const char* src = nullptr;
+    char* dst = nullptr;
+    uint32_t len = 0;
+    char* const orow = row_ok ? T.out + row * (uint64_t)a.row_bytes : nullptr;
+    if (bad && sidx == 0) {
+      len = a.row_bytes;  // zero row
+      dst = orow;
+    } else if (pinned && sidx == 0) {
+      src = a.cpu.buf + cpu_slot * a.cpu.stride;
+      dst = orow;
+      len = a.row_bytes;
+    } else if (seg_ok) {
+      const uint64_t in_page = (b0 + s0) - (p << shift);
+      if (gcls == CLS_BYPASS)
+        src = backing_addr(a.b, p, shift) + in_page;
+      else
+        src = a.c.slots + (gslot << shift) + in_page;
+      dst = orow + s0;
+      len = s1 - s0;
+    }
+    const unsigned has = __ballot_sync(0xffffffffu, len != 0);
+    const int pos = __popc(has & ((1u << lane) - 1u));
+    if (len) sd[pos] = SegDesc{src, dst, len, 0u};
+    __syncwarp();
+    copy_segments<VEC>(sd, __popc(has), lane);
+    __syncwarp();
+
+    // ---- release, clock reference bit, window-buffer consumption
+    if (took_ref) {
+      red_add_release(stw, (unsigned long long)(-(long long)cnt));
+      if (gcls != CLS_BYPASS) a.c.slot_ref[gslot] = 1;
+      if (a.c.wb) wb_consume(a.c.wb + p, cnt);
+    }
+
+    // ---- counters
+    if (bad && sidx == 0) *reinterpret_cast<volatile int*>(a.host_err) = 1;
+    const unsigned r0 = sidx == 0;
+    const unsigned n_rows_c = __popc(__ballot_sync(0xffffffffu, row_ok && r0));
+    const unsigned n_cpu = __popc(__ballot_sync(0xffffffffu, pinned && r0));
+    const unsigned n_bad = __popc(__ballot_sync(0xffffffffu, bad && r0));
+    const unsigned n_acc = __popc(__ballot_sync(0xffffffffu, seg_ok));
+    const unsigned n_hit = __popc(__ballot_sync(0xffffffffu, seg_ok && gcls == CLS_HIT));
+    const unsigned n_miss = __popc(__ballot_sync(0xffffffffu, seg_ok && (gcls == CLS_OWN || gcls == CLS_WAITED)));
+    const unsigned n_byp = __popc(__ballot_sync(0xffffffffu, seg_ok && gcls == CLS_BYPASS));
+    const unsigned lh = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_HIT ? len : 0u);
+    const unsigned lm = __reduce_add_sync(0xffffffffu, seg_ok && (gcls == CLS_OWN || gcls == CLS_WAITED) ? len : 0u);
+    const unsigned lb = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_BYPASS ? len : 0u);
+    const unsigned lc = __reduce_add_sync(0xffffffffu, pinned && r0 ? len : 0u);
+    if (lane == 0) {
+      acc[K_ROWS] += n_rows_c;
+      acc[K_CPU] += n_cpu;
+      acc[K_BAD] += n_bad;
+      acc[K_ACCESS] += n_acc;
+      acc[K_HIT] += n_hit;
+      acc[K_MISS] += n_miss;
+      acc[K_BYPASS] += n_byp;
+      acc[K_BHIT] += lh;
+      acc[K_BMISS] += lm;
+      acc[K_BBYP] += lb;
+      acc[K_BCPU] += lc;
+    }
+    __syncwarp();
+  }
+
+  __syncwarp();
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < K_N; i++)
+      if (acc[i]) atomicAdd(a.stats + kStatMap[i], acc[i]);
+  }
+}
+
+// Window buffering: one thread per node id, +1 on the pin counter of every
+// page its row touches (gids_kernel.cu:246-256 marks one page per id).
+__global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
+  const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.n) return;
+  const int64_t id = a.idx[i];
+  const int64_t rs = id + a.off;
+  if (id < 0 || rs < 0 || (uint64_t)rs >= a.n_rows) return;  // the gather reports bad ids
+  const uint64_t b0 = (uint64_t)rs * a.stride;
+  const uint64_t p0 = b0 >> a.page_shift, p1 = (b0 + a.row_bytes - 1) >> a.page_shift;
+  for (uint64_t p = p0; p <= p1; p++) atomicAdd(a.wb + p, 1u);
+}
+
+}  // namespace
+
+void launch_gather(const GatherArgs& a, int vec, int grid, cudaStream_t st) {
+  switch (vec) {
+    case 16: gather_kernel<16><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 8: gather_kernel<8><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 4: gather_kernel<4><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 2: gather_kernel<2><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    default: throw Error(GIDS_E_INVAL, "unsupported vector width");
+  }
+  GIDS_CUDA(cudaGetLastError());
+}
+
+int gather_blocks_per_sm(int vec) {
+  int n = 0;
+  switch (vec) {
+    case 16: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<16>, GATHER_THREADS, 0)); break;
+    case 8: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<8>, GATHER_THREADS, 0)); break;
+    case 4: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<4>, GATHER_THREADS, 0)); break;
+    case 2: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<2>, GATHER_THREADS, 0)); break;
+    default: throw Error(GIDS_E_INVAL, "unsupported vector width");
+  }
+  return n;
+}
+
+void launch_wb_mark(const WbArgs& a, cudaStream_t st) {
+  if (!a.n) return;
+  const unsigned blocks = (unsigned)((a.n + 255) / 256);
+  wb_mark_kernel<<<blocks, 256, 0, st>>>(a);
+  GIDS_CUDA(cudaGetLastError());
+}
+
+}  // namespace gids

@@ -1,0 +1,273 @@
+// Internal declarations shared by the device code (gather.cu), the store
+// (store.cu), the emulated SSDs (backing.cpp) and the C ABI (abi.cpp).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gids_b200.h"
+
+namespace gids {
+
+// ------------------------------------------------------------------ errors
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+void set_last_error(const std::string& msg);
+void clear_last_error();
+
+#define GIDS_CUDA(call)                                                                                 \
+  do {                                                                                                  \
+    cudaError_t e_ = (call);                                                                            \
+    if (e_ != cudaSuccess)                                                                              \
+      throw ::gids::Error(GIDS_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_) + " (" +     \
+                                           __FILE__ + ":" + std::to_string(__LINE__) + ")");           \
+  } while (0)
+#define GIDS_CHECK(cond, code, msg)                     \
+  do {                                                  \
+    if (!(cond)) throw ::gids::Error((code), (msg));    \
+  } while (0)
+
+// RAII guard: switch to the store's device for the duration of a call.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) GIDS_CUDA(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() {
+    int cur;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// -------------------------------------------------------- page state word
+// One 64-bit word per page of the range (the page table). It plays the role
+// of the reference's data_page_t state word (page_cache_backup.h:104-117,
+// 143-152): a reference count in the low bits, BUSY while a fill is in
+// flight, VALID once the page is resident, and the cache slot that holds the
+// page in the high 32 bits.
+constexpr uint64_t ST_REF_MASK = (1ull << 24) - 1;
+constexpr uint64_t ST_BUSY = 1ull << 24;
+constexpr uint64_t ST_VALID = 1ull << 25;
+constexpr int ST_SLOT_SHIFT = 32;
+constexpr uint64_t SLOT_EMPTY = ~0ull;
+
+// Per-segment source classes used by the gather kernel and its counters.
+enum : int { CLS_NONE = 0, CLS_HIT = 1, CLS_OWN = 2, CLS_WAIT = 3, CLS_WAITED = 4, CLS_BYPASS = 5 };
+
+// ---------------------------------------------------- device-side views
+struct DevCache {
+  unsigned long long* state;      // [n_pages] page table
+  unsigned long long* slot_page;  // [n_slots] page held by each slot (SLOT_EMPTY if none)
+  unsigned char* slot_ref;        // [n_slots] clock reference bit
+  unsigned int* wb;               // [n_pages] window-buffer pins, or nullptr
+  char* slots;                    // [n_slots * page_size] resident pages
+  unsigned long long* clock;      // clock hand
+  uint64_t n_slots;
+  uint64_t n_pages;
+  uint32_t page_shift;
+  uint32_t page_size;
+};
+
+struct DevBacking {
+  const char* ssd[GIDS_MAX_SSD];  // device addresses of the mapped SSD regions
+  uint32_t n_ssd;
+  uint64_t page_start;  // first page of the range on every SSD
+  uint64_t wrap_pages;  // pages physically held (== n_pages when the SSDs hold the whole range)
+};
+
+struct DevCpuBuf {
+  int mode;  // 0 = none, 1 = rows [0, seq_len) (seq mode), 2 = bitmap
+  uint64_t seq_len;
+  const unsigned long long* bits;  // [nwords] membership bitmap over rows
+  const unsigned int* rank;        // [nwords] pinned rows before each word
+  uint64_t nwords;
+  const char* buf;  // device address of the mapped pinned buffer
+  uint64_t stride;  // bytes between buffer rows
+  uint32_t row_bytes;  // bytes held per buffer row
+};
+
+struct GatherTuple {
+  const int64_t* idx;
+  char* out;
+  uint64_t n;
+  uint64_t key_off;
+  uint64_t chunk_begin;  // first chunk of this tuple in the launch
+};
+
+struct GatherArgs {
+  DevCache c;
+  DevBacking b;
+  DevCpuBuf cpu;
+  unsigned long long* stats;  // [GIDS_STAT_COUNT]
+  int* host_err;              // mapped pinned host word, set to 1 on a bad id
+  uint64_t src_stride;        // bytes between rows of the range (cache_dim * elem_bytes)
+  uint64_t n_rows;            // rows that lie completely inside the range
+  uint32_t row_bytes;         // bytes gathered per row (dim * elem_bytes)
+  uint32_t seg_shift;         // log2(page segments per row lane group)
+  uint32_t spin_limit;        // bounded wait for another warp's fill
+  uint32_t sweep_limit;       // bounded clock sweep (rounds of 32 candidates)
+  int k;
+  uint64_t total_chunks;
+  GatherTuple t[GIDS_MAX_TUPLES];
+};
+
+struct WbArgs {
+  unsigned int* wb;
+  const int64_t* idx;
+  uint64_t n;
+  int64_t off;
+  uint64_t stride;  // bytes per row of the range
+  uint64_t row_bytes;
+  uint64_t n_rows;
+  uint32_t page_shift;
+};
+
+// Launchers (gather.cu).
+void launch_gather(const GatherArgs& a, int vec, int grid, cudaStream_t st);
+void launch_wb_mark(const WbArgs& a, cudaStream_t st);
+void launch_invalidate_all(const DevCache& c, cudaStream_t st);
+int gather_blocks_per_sm(int vec);
+constexpr int GATHER_THREADS = 256;
+
+// ------------------------------------------------------- emulated SSDs
+struct SsdRegion {
+  char* host = nullptr;
+  char* dev = nullptr;  // device address of the mapped region
+  uint64_t bytes = 0;
+  int fd = -1;
+  bool registered = false;
+  std::string path;
+};
+
+class Controllers {
+ public:
+  ~Controllers();
+  void init(uint32_t n, uint64_t q_depth, uint64_t n_queues, const int32_t* ssd_list);
+  void set_emulation(uint64_t capacity_per_ssd, const char* pattern);
+  // Size and map the first n_ssd SSDs for a range of range_pages pages with
+  // page_size bytes, starting at page_start on each SSD. Returns the wrap
+  // period in pages.
+  uint64_t bind(uint32_t n_ssd, uint32_t page_size, uint64_t page_start, uint64_t range_pages);
+  void register_with_cuda();
+  std::vector<SsdRegion> ssd;
+  std::vector<int32_t> ssd_list;
+  uint32_t n_ctrls = 0;
+  uint64_t q_depth = 0, n_queues = 0;
+  uint64_t capacity_per_ssd = 0;
+  std::string pattern;
+  uint32_t page_size = 0;
+  uint64_t page_start = 0, range_pages = 0, wrap_pages = 0;
+  uint32_t n_bound = 0;
+  bool bound = false;
+};
+
+// Striped host I/O over the bound SSDs (backing.cpp). Offsets are bytes of
+// the logical range.
+void backing_write(Controllers& c, const void* src, uint64_t nbytes, uint64_t off);
+void backing_read(const Controllers& c, void* dst, uint64_t nbytes, uint64_t off);
+void backing_fill_synthetic(Controllers& c, int kind, uint64_t seed, int threads);
+int synth_elem_bytes(int kind);
+// Host pointer of logical page p (after wrap).
+const char* backing_page_host(const Controllers& c, uint64_t p);
+
+// Pinned, GPU-mapped host allocation (mmap + transparent huge pages +
+// cudaHostRegister), which pins far faster than cudaHostAlloc at tens of GB.
+struct PinnedHost {
+  char* host = nullptr;
+  char* dev = nullptr;
+  uint64_t bytes = 0;
+  void alloc(uint64_t bytes, int threads);
+  void release();
+  ~PinnedHost() { release(); }
+};
+void parallel_for(uint64_t n, int threads, const std::function<void(uint64_t, uint64_t)>& fn);
+
+// ---------------------------------------------------------------- store
+class Store {
+ public:
+  Store(uint32_t elem_bytes, int device);
+  ~Store();
+  void init_controllers(Controllers* c, uint32_t page_size, uint64_t read_off_pages, uint64_t cache_mb,
+                        uint64_t num_ele, uint64_t num_ssd);
+  void read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
+                  int cache_dim, const uint64_t* key_offs, cudaStream_t st);
+  void window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st);
+  void cpu_backing_buffer(uint64_t dim, uint64_t len);
+  void set_cpu_buffer(const int64_t* host_idx, int64_t num);
+  void set_row_layout(uint32_t cache_dim);
+  void store_tensor(const void* src, uint64_t num_rows, uint64_t offset_bytes);
+  void write_range(const void* src, uint64_t nbytes, uint64_t off);
+  void flush_cache();
+  void get_stats(uint64_t* out, int count);
+  void reset_stats();
+  void print_stats();
+  double kernel_time_ms();
+  void synchronize();
+  uint32_t cpu_access_count();
+  void flush_cpu_access_count();
+
+  uint32_t elem_bytes;
+  int device;
+  bool synchronous = true;
+  Controllers* ctrls = nullptr;
+  bool initialized = false;
+  uint32_t page_size = 0, page_shift = 0;
+  uint64_t read_off_pages = 0, num_ele = 0, range_bytes = 0, n_pages = 0, n_slots = 0;
+  uint32_t row_layout = 0;  // source row stride (elements) for CPU-buffer fills / WB; 0 = unknown
+
+  // device allocations
+  unsigned long long* d_state = nullptr;
+  unsigned long long* d_slot_page = nullptr;
+  unsigned char* d_slot_ref = nullptr;
+  unsigned int* d_wb = nullptr;
+  char* d_slots = nullptr;
+  unsigned long long* d_clock = nullptr;
+  unsigned long long* d_stats = nullptr;
+  int* h_err = nullptr;  // mapped pinned host word
+  int* d_err = nullptr;
+
+  // constant CPU buffer
+  PinnedHost cpu_buf;
+  uint64_t cpu_dim = 0, cpu_len = 0;
+  int cpu_mode = 0;
+  std::vector<int64_t> cpu_rows;  // sorted pinned rows (bitmap mode)
+  unsigned long long* d_cpu_bits = nullptr;
+  unsigned int* d_cpu_rank = nullptr;
+  uint64_t cpu_nwords = 0;
+  uint32_t cpu_filled_stride = 0;  // source stride (elements) the buffer was filled with; 0 = not filled
+  void fill_cpu_buffer(uint32_t src_stride_elems);
+
+  // counters and timing
+  uint64_t stat_base_cpu = 0;  // CPU-row counter at the last flush_cpu_access_count
+  uint32_t cpu_access_host = 0;
+  cudaStream_t last_stream = nullptr;
+  struct EvPair {
+    cudaEvent_t a, b;
+  };
+  std::vector<EvPair> ev_pending, ev_free;
+  double kernel_ms = 0.0;
+  uint64_t total_access = 0;
+  uint64_t launches = 0;
+  void fold_events(bool wait);
+  int grid_blocks[5] = {0, 0, 0, 0, 0};
+  std::mutex mu;
+
+ private:
+  void free_all();
+  DevCache dev_cache() const;
+  DevBacking dev_backing() const;
+  DevCpuBuf dev_cpu() const;
+  void check_async_error();
+};
+
+}  // namespace gids

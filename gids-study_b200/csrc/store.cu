@@ -1,0 +1,534 @@
+// Host side of one feature store: the page cache in HBM, the constant CPU
+// buffer, window buffering, counters and launches. Mirrors the members of the
+// reference's BAM_Feature_Store<T> (gids_module/include/bam_nvme.h:230-613,
+// gids_module/gids_nvme.cu:123-806).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cinttypes>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+
+#include "gids_internal.hpp"
+
+namespace gids {
+
+namespace {
+uint32_t log2_exact(uint64_t v) {
+  uint32_t s = 0;
+  while ((1ull << s) < v) s++;
+  return s;
+}
+uint64_t gcd64(uint64_t a, uint64_t b) {
+  while (b) {
+    uint64_t t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+int host_threads() {
+  unsigned n = std::thread::hardware_concurrency();
+  return n ? (int)n : 1;
+}
+}  // namespace
+
+Store::Store(uint32_t eb, int dev) : elem_bytes(eb), device(dev) {
+  GIDS_CHECK(eb == 2 || eb == 4 || eb == 8, GIDS_E_INVAL, "elem_bytes must be 2, 4 or 8");
+  int n = 0;
+  GIDS_CUDA(cudaGetDeviceCount(&n));
+  GIDS_CHECK(dev >= 0 && dev < n, GIDS_E_INVAL, "device " + std::to_string(dev) + " not present");
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaMalloc(&d_stats, GIDS_STAT_COUNT * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_stats, 0, GIDS_STAT_COUNT * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMalloc(&d_clock, sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_clock, 0, sizeof(unsigned long long)));
+  GIDS_CUDA(cudaHostAlloc(&h_err, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+  *h_err = 0;
+  GIDS_CUDA(cudaHostGetDevicePointer(&d_err, h_err, 0));
+}
+
+Store::~Store() {
+  try {
+    DeviceGuard g(device);
+    cudaDeviceSynchronize();
+    free_all();
+    for (auto& e : ev_pending) {
+      cudaEventDestroy(e.a);
+      cudaEventDestroy(e.b);
+    }
+    for (auto& e : ev_free) {
+      cudaEventDestroy(e.a);
+      cudaEventDestroy(e.b);
+    }
+    if (d_stats) cudaFree(d_stats);
+    if (d_clock) cudaFree(d_clock);
+    if (h_err) cudaFreeHost(h_err);
+  } catch (...) {
+  }
+}
+
+void Store::free_all() {
+  auto f = [](auto*& p) {
+    if (p) cudaFree((void*)p);
+    p = nullptr;
+  };
+  f(d_state);
+  f(d_slot_page);
+  f(d_slot_ref);
+  f(d_wb);
+  f(d_slots);
+  f(d_cpu_bits);
+  f(d_cpu_rank);
+  cpu_buf.release();
+}
+
+void Store::init_controllers(Controllers* c, uint32_t ps, uint64_t read_off_pages_, uint64_t cache_mb, uint64_t ne,
+                             uint64_t num_ssd) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(c, GIDS_E_INVAL, "controllers are null");
+  GIDS_CHECK(!initialized, GIDS_E_STATE, "init_controllers called twice");
+  GIDS_CHECK(ps >= 512 && (ps & (ps - 1)) == 0, GIDS_E_INVAL, "page_size must be a power of two >= 512");
+  GIDS_CHECK(ne > 0, GIDS_E_INVAL, "num_ele must be > 0");
+  GIDS_CHECK(num_ssd >= 1 && num_ssd <= c->n_ctrls && num_ssd <= GIDS_MAX_SSD, GIDS_E_INVAL,
+             "num_ssd must be in [1, controllers initialised]");
+  DeviceGuard g(device);
+  page_size = ps;
+  page_shift = log2_exact(ps);
+  read_off_pages = read_off_pages_;
+  num_ele = ne;
+  range_bytes = ne * elem_bytes;
+  n_pages = (range_bytes + ps - 1) / ps;
+  n_slots = cache_mb * (1ull << 20) / ps;
+  GIDS_CHECK(n_slots < (1ull << 32) - 1, GIDS_E_INVAL, "cache too large for 32-bit slot numbers");
+
+  c->bind((uint32_t)num_ssd, ps, read_off_pages, n_pages);
+  c->register_with_cuda();
+  ctrls = c;
+
+  GIDS_CUDA(cudaMalloc(&d_state, n_pages * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_state, 0, n_pages * sizeof(unsigned long long)));
+  if (n_slots) {
+    GIDS_CUDA(cudaMalloc(&d_slot_page, n_slots * sizeof(unsigned long long)));
+    GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
+    GIDS_CUDA(cudaMalloc(&d_slot_ref, n_slots));
+    GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
+    GIDS_CUDA(cudaMalloc(&d_slots, n_slots * (uint64_t)ps));
+  }
+  int sms = 0;
+  GIDS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  const int vecs[4] = {16, 8, 4, 2};
+  for (int i = 0; i < 4; i++) grid_blocks[i] = std::max(1, gather_blocks_per_sm(vecs[i])) * sms;
+  GIDS_CUDA(cudaDeviceSynchronize());
+  initialized = true;
+}
+
+DevCache Store::dev_cache() const {
+  DevCache c{};
+  c.state = d_state;
+  c.slot_page = d_slot_page;
+  c.slot_ref = d_slot_ref;
+  c.wb = d_wb;
+  c.slots = d_slots;
+  c.clock = d_clock;
+  c.n_slots = n_slots;
+  c.n_pages = n_pages;
+  c.page_shift = page_shift;
+  c.page_size = page_size;
+  return c;
+}
+
+DevBacking Store::dev_backing() const {
+  DevBacking b{};
+  for (uint32_t i = 0; i < ctrls->n_bound; i++) b.ssd[i] = ctrls->ssd[i].dev;
+  b.n_ssd = ctrls->n_bound;
+  b.page_start = ctrls->page_start;
+  b.wrap_pages = ctrls->wrap_pages;
+  return b;
+}
+
+DevCpuBuf Store::dev_cpu() const {
+  DevCpuBuf d{};
+  d.mode = cpu_filled_stride ? cpu_mode : 0;
+  d.seq_len = cpu_len;
+  d.bits = d_cpu_bits;
+  d.rank = d_cpu_rank;
+  d.nwords = cpu_nwords;
+  d.buf = cpu_buf.dev;
+  d.stride = cpu_buf.bytes && cpu_len ? cpu_buf.bytes / cpu_len : 0;
+  d.row_bytes = (uint32_t)(cpu_dim * elem_bytes);
+  return d;
+}
+
+void Store::check_async_error() {
+  if (h_err && *reinterpret_cast<volatile int*>(h_err)) {
+    *reinterpret_cast<volatile int*>(h_err) = 0;
+    throw Error(GIDS_E_RANGE, "a node id addressed a row outside the feature range (its output row is zero)");
+  }
+}
+
+void Store::fold_events(bool wait) {
+  size_t keep = 0;
+  for (size_t i = 0; i < ev_pending.size(); i++) {
+    auto& e = ev_pending[i];
+    cudaError_t q = wait ? cudaEventSynchronize(e.b) : cudaEventQuery(e.b);
+    if (q == cudaSuccess) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, e.a, e.b) == cudaSuccess) kernel_ms += ms;
+      ev_free.push_back(e);
+    } else {
+      if (q != cudaErrorNotReady) GIDS_CUDA(q);
+      ev_pending[keep++] = e;
+    }
+  }
+  ev_pending.resize(keep);
+}
+
+void Store::set_row_layout(uint32_t cache_dim) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(cache_dim > 0, GIDS_E_INVAL, "cache_dim must be > 0");
+  row_layout = cache_dim;
+  if (initialized && cpu_mode && cpu_filled_stride != cache_dim) fill_cpu_buffer(cache_dim);
+}
+
+void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
+                       int cache_dim, const uint64_t* key_offs, cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "read_feature before init_controllers");
+  GIDS_CHECK(k >= 0, GIDS_E_INVAL, "k must be >= 0");
+  GIDS_CHECK(dim > 0 && cache_dim > 0 && dim <= cache_dim, GIDS_E_INVAL, "need 0 < dim <= cache_dim");
+  DeviceGuard g(device);
+  check_async_error();
+  fold_events(false);
+  const uint64_t row_bytes = (uint64_t)dim * elem_bytes;
+  const uint64_t src_stride = (uint64_t)cache_dim * elem_bytes;
+  GIDS_CHECK(row_bytes < (1ull << 31), GIDS_E_INVAL, "row too large");
+  if (cpu_mode) {
+    GIDS_CHECK((uint64_t)dim <= cpu_dim, GIDS_E_INVAL,
+               "dim exceeds the constant CPU buffer's row width (cpu_backing_buffer dim)");
+    if (cpu_filled_stride != (uint32_t)cache_dim) fill_cpu_buffer((uint32_t)cache_dim);
+  }
+  if (!row_layout) row_layout = (uint32_t)cache_dim;
+
+  // lanes per row: pages one row can touch, rounded up to a power of two
+  const uint64_t gst = gcd64(src_stride, page_size);
+  const uint64_t max_pages = (page_size - gst + row_bytes - 1) / page_size + 1;
+  uint32_t seg_shift = 0;
+  while ((1ull << seg_shift) < max_pages) seg_shift++;
+  GIDS_CHECK(seg_shift <= 5, GIDS_E_UNSUPPORTED, "a row may span more than 32 pages; use larger pages");
+  const uint64_t rpc = 32ull >> seg_shift;
+
+  // vector width: every address and length of the copy must be a multiple
+  int vec = 16;
+  auto fits = [&](uint64_t v) { return v % vec == 0; };
+  while (vec > 2 && !(fits(row_bytes) && fits(src_stride))) vec >>= 1;
+  for (int i = 0; i < k; i++)
+    while (vec > 2 && (uint64_t)(uintptr_t)outs[i] % vec) vec >>= 1;
+  GIDS_CHECK(row_bytes % vec == 0 && src_stride % vec == 0, GIDS_E_INVAL, "rows must be 2-byte aligned");
+  for (int i = 0; i < k; i++) {
+    GIDS_CHECK(ns[i] == 0 || (outs[i] && idxs[i]), GIDS_E_INVAL, "null output or index pointer");
+    GIDS_CHECK((uintptr_t)idxs[i] % 8 == 0 || ns[i] == 0, GIDS_E_INVAL, "index array must be 8-byte aligned");
+    GIDS_CHECK((uintptr_t)outs[i] % vec == 0 || ns[i] == 0, GIDS_E_INVAL, "output not aligned");
+  }
+
+  GatherArgs a;
+  memset(&a, 0, sizeof(a));
+  a.c = dev_cache();
+  a.b = dev_backing();
+  a.cpu = dev_cpu();
+  a.stats = d_stats;
+  a.host_err = d_err;
+  a.src_stride = src_stride;
+  a.n_rows = range_bytes >= row_bytes ? (range_bytes - row_bytes) / src_stride + 1 : 0;
+  a.row_bytes = (uint32_t)row_bytes;
+  a.seg_shift = seg_shift;
+  a.spin_limit = 1u << 16;
+  a.sweep_limit = 64;
+  uint64_t rows_total = 0;
+  for (int base = 0; base < k || (k == 0 && base == 0); base += GIDS_MAX_TUPLES) {
+    const int kk = std::min(GIDS_MAX_TUPLES, k - base);
+    uint64_t chunks = 0;
+    int used = 0;
+    for (int i = 0; i < kk; i++) {
+      const uint64_t n = ns[base + i];
+      if (!n) continue;
+      GatherTuple& t = a.t[used++];
+      t.idx = idxs[base + i];
+      t.out = (char*)outs[base + i];
+      t.n = n;
+      t.key_off = key_offs ? key_offs[base + i] : 0;
+      t.chunk_begin = chunks;
+      chunks += (n + rpc - 1) / rpc;
+      rows_total += n;
+    }
+    if (!chunks) {
+      if (k == 0) break;
+      continue;
+    }
+    a.k = used;
+    a.total_chunks = chunks;
+    const int vi = vec == 16 ? 0 : vec == 8 ? 1 : vec == 4 ? 2 : 3;
+    const uint64_t want_blocks = (chunks + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
+    const int grid = (int)std::min<uint64_t>(want_blocks, (uint64_t)grid_blocks[vi]);
+    EvPair ev;
+    if (!ev_free.empty()) {
+      ev = ev_free.back();
+      ev_free.pop_back();
+    } else {
+      GIDS_CUDA(cudaEventCreate(&ev.a));
+      GIDS_CUDA(cudaEventCreate(&ev.b));
+    }
+    GIDS_CUDA(cudaEventRecord(ev.a, st));
+    launch_gather(a, vec, grid, st);
+    launches++;
+    GIDS_CUDA(cudaEventRecord(ev.b, st));
+    ev_pending.push_back(ev);
+    if (k == 0) break;
+  }
+  total_access += rows_total;
+  last_stream = st;
+  if (synchronous) {
+    GIDS_CUDA(cudaStreamSynchronize(st));
+    fold_events(true);
+    check_async_error();
+  }
+}
+
+void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "set_window_buffering before init_controllers");
+  GIDS_CHECK(n >= 0, GIDS_E_INVAL, "n must be >= 0");
+  if (n == 0) return;
+  GIDS_CHECK(idx, GIDS_E_INVAL, "null index pointer");
+  DeviceGuard g(device);
+  if (!d_wb) {
+    GIDS_CUDA(cudaMalloc(&d_wb, n_pages * sizeof(unsigned int)));
+    GIDS_CUDA(cudaMemset(d_wb, 0, n_pages * sizeof(unsigned int)));
+  }
+  // rows map to pages by bytes; without a known layout, one row per page
+  // (the reference's assumption, gids_kernel.cu:251-252)
+  uint32_t se = stride_elems ? stride_elems : row_layout ? row_layout : page_size / elem_bytes;
+  WbArgs w{};
+  w.wb = d_wb;
+  w.idx = idx;
+  w.n = (uint64_t)n;
+  w.off = off;
+  w.stride = (uint64_t)se * elem_bytes;
+  w.row_bytes = w.stride;
+  w.n_rows = range_bytes >= w.row_bytes ? (range_bytes - w.row_bytes) / w.stride + 1 : 0;
+  w.page_shift = page_shift;
+  launch_wb_mark(w, st);
+  last_stream = st;
+  if (synchronous) GIDS_CUDA(cudaStreamSynchronize(st));
+}
+
+void Store::cpu_backing_buffer(uint64_t dim, uint64_t len) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "cpu_backing_buffer before init_controllers");
+  GIDS_CHECK(dim > 0, GIDS_E_INVAL, "dim must be > 0");
+  DeviceGuard g(device);
+  cudaDeviceSynchronize();
+  cpu_buf.release();
+  const uint64_t stride = (dim * elem_bytes + 15) / 16 * 16;
+  cpu_dim = dim;
+  cpu_len = len;
+  cpu_rows.clear();
+  cpu_mode = len ? 1 : 0;  // seq mode until set_cpu_buffer
+  cpu_filled_stride = 0;
+  if (len) cpu_buf.alloc(stride * len, host_threads());
+  if (cpu_mode && row_layout) fill_cpu_buffer(row_layout);
+}
+
+void Store::set_cpu_buffer(const int64_t* idx, int64_t num) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "set_cpu_buffer before init_controllers");
+  GIDS_CHECK(cpu_buf.bytes || num == 0, GIDS_E_STATE, "set_cpu_buffer before cpu_backing_buffer");
+  GIDS_CHECK(num >= 0 && (uint64_t)num <= cpu_len, GIDS_E_INVAL, "more pinned rows than the CPU buffer holds");
+  GIDS_CHECK(num == 0 || idx, GIDS_E_INVAL, "null index pointer");
+  DeviceGuard g(device);
+  cudaDeviceSynchronize();
+  std::vector<int64_t> rows(idx, idx + num);
+  std::sort(rows.begin(), rows.end());
+  rows.erase(std::unique(rows.begin(), rows.end()), rows.end());
+  GIDS_CHECK(rows.empty() || rows.front() >= 0, GIDS_E_RANGE, "negative node id in the pin list");
+  cpu_rows = std::move(rows);
+  // membership bitmap over rows [0, max pinned row], and the rank of each word
+  cpu_nwords = cpu_rows.empty() ? 0 : (uint64_t)(cpu_rows.back() >> 6) + 1;
+  std::vector<unsigned long long> bits(cpu_nwords, 0ull);
+  std::vector<unsigned int> rank(cpu_nwords, 0u);
+  for (int64_t r : cpu_rows) bits[r >> 6] |= 1ull << (r & 63);
+  unsigned int acc = 0;
+  for (uint64_t w = 0; w < cpu_nwords; w++) {
+    rank[w] = acc;
+    acc += (unsigned int)__builtin_popcountll(bits[w]);
+  }
+  if (d_cpu_bits) cudaFree(d_cpu_bits);
+  if (d_cpu_rank) cudaFree(d_cpu_rank);
+  d_cpu_bits = nullptr;
+  d_cpu_rank = nullptr;
+  if (cpu_nwords) {
+    GIDS_CUDA(cudaMalloc(&d_cpu_bits, cpu_nwords * sizeof(unsigned long long)));
+    GIDS_CUDA(cudaMalloc(&d_cpu_rank, cpu_nwords * sizeof(unsigned int)));
+    GIDS_CUDA(cudaMemcpy(d_cpu_bits, bits.data(), cpu_nwords * 8, cudaMemcpyHostToDevice));
+    GIDS_CUDA(cudaMemcpy(d_cpu_rank, rank.data(), cpu_nwords * 4, cudaMemcpyHostToDevice));
+  }
+  cpu_mode = 2;
+  cpu_filled_stride = 0;
+  if (row_layout) fill_cpu_buffer(row_layout);
+}
+
+// Copies the pinned rows from the backing store into the CPU buffer (host
+// threads; the buffer and the emulated SSDs are both host memory). The
+// reference fills through the GPU cache with one block per row
+// (set_cpu_buffer_data_kernel, gids_kernel.cu:216-228).
+void Store::fill_cpu_buffer(uint32_t src_stride_elems) {
+  const uint64_t stride = cpu_len ? cpu_buf.bytes / cpu_len : 0;
+  const uint64_t src_stride = (uint64_t)src_stride_elems * elem_bytes;
+  const uint64_t row_bytes = cpu_dim * elem_bytes;
+  const uint64_t n_rows = range_bytes >= row_bytes ? (range_bytes - row_bytes) / src_stride + 1 : 0;
+  const uint64_t count = cpu_mode == 1 ? cpu_len : cpu_rows.size();
+  if (cpu_mode == 2 && !cpu_rows.empty())
+    GIDS_CHECK((uint64_t)cpu_rows.back() < n_rows, GIDS_E_RANGE, "pinned node id outside the feature range");
+  const uint64_t lim = cpu_mode == 1 ? std::min<uint64_t>(count, n_rows) : count;
+  parallel_for(lim, host_threads(), [&](uint64_t lo, uint64_t hi) {
+    for (uint64_t k = lo; k < hi; k++) {
+      const uint64_t r = cpu_mode == 1 ? k : (uint64_t)cpu_rows[k];
+      backing_read(*ctrls, cpu_buf.host + k * stride, row_bytes, r * src_stride);
+    }
+  });
+  if (cpu_mode == 1 && lim < cpu_len) cpu_len = lim;  // seq rows past the range are never pinned
+  cpu_filled_stride = src_stride_elems;
+}
+
+void Store::store_tensor(const void* src, uint64_t num_rows, uint64_t offset_bytes) {
+  // gids_nvme.cu:616-663 + gids_kernel.cu:378-389: row r (of page_size /
+  // elem_bytes elements) of the range gets elements [r*dim + off, (r+1)*dim +
+  // off) of src, off = offset_bytes / elem_bytes.
+  const uint64_t dim = page_size / elem_bytes;
+  const uint64_t nbytes = num_rows * dim * elem_bytes;
+  const uint64_t src_off = offset_bytes / elem_bytes * elem_bytes;
+  write_range((const char*)src + src_off, nbytes, 0);
+}
+
+void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "write before init_controllers");
+  GIDS_CHECK(off + nbytes <= (uint64_t)n_pages * page_size, GIDS_E_RANGE, "write past the end of the range");
+  if (!nbytes) return;
+  GIDS_CHECK(src, GIDS_E_INVAL, "null source");
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaDeviceSynchronize());
+  cudaPointerAttributes attr{};
+  GIDS_CUDA(cudaPointerGetAttributes(&attr, src));
+  if (attr.type == cudaMemoryTypeDevice) {
+    // stage device data through a pinned bounce buffer
+    const uint64_t chunk = 256ull << 20;
+    char* bounce = nullptr;
+    GIDS_CUDA(cudaMallocHost(&bounce, std::min(chunk, nbytes)));
+    try {
+      for (uint64_t done = 0; done < nbytes; done += chunk) {
+        const uint64_t len = std::min(chunk, nbytes - done);
+        GIDS_CUDA(cudaMemcpy(bounce, (const char*)src + done, len, cudaMemcpyDeviceToHost));
+        backing_write(*ctrls, bounce, len, off + done);
+      }
+    } catch (...) {
+      cudaFreeHost(bounce);
+      throw;
+    }
+    cudaFreeHost(bounce);
+  } else {
+    backing_write(*ctrls, src, nbytes, off);
+  }
+  // the cache and the CPU buffer may hold stale copies of the written pages
+  GIDS_CUDA(cudaMemset(d_state, 0, n_pages * sizeof(unsigned long long)));
+  if (n_slots) {
+    GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
+    GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
+  }
+  if (cpu_mode && cpu_filled_stride) fill_cpu_buffer(cpu_filled_stride);
+  GIDS_CUDA(cudaDeviceSynchronize());
+}
+
+void Store::flush_cache() {
+  // The cache never holds dirty pages (writes go straight to the backing
+  // store), so flushing only has to drop every resident page.
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "flush_cache before init_controllers");
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaDeviceSynchronize());
+  GIDS_CUDA(cudaMemset(d_state, 0, n_pages * sizeof(unsigned long long)));
+  if (n_slots) {
+    GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
+    GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
+  }
+  GIDS_CUDA(cudaDeviceSynchronize());
+}
+
+void Store::synchronize() {
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaDeviceSynchronize());
+  fold_events(true);
+  check_async_error();
+}
+
+void Store::get_stats(uint64_t* out, int count) {
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaDeviceSynchronize());
+  unsigned long long h[GIDS_STAT_COUNT];
+  GIDS_CUDA(cudaMemcpy(h, d_stats, sizeof(h), cudaMemcpyDeviceToHost));
+  h[GIDS_STAT_LAUNCHES] = launches;
+  for (int i = 0; i < count && i < GIDS_STAT_COUNT; i++) out[i] = h[i];
+}
+
+void Store::reset_stats() {
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaDeviceSynchronize());
+  GIDS_CUDA(cudaMemset(d_stats, 0, GIDS_STAT_COUNT * sizeof(unsigned long long)));
+  fold_events(true);
+  kernel_ms = 0.0;
+  total_access = 0;
+  launches = 0;
+  stat_base_cpu = 0;
+}
+
+double Store::kernel_time_ms() {
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceGuard g(device);
+  fold_events(true);
+  return kernel_ms;
+}
+
+uint32_t Store::cpu_access_count() {
+  uint64_t s[GIDS_STAT_COUNT];
+  get_stats(s, GIDS_STAT_COUNT);
+  return (uint32_t)(s[GIDS_STAT_CPU_ROWS] - stat_base_cpu);
+}
+
+void Store::flush_cpu_access_count() {
+  uint64_t s[GIDS_STAT_COUNT];
+  get_stats(s, GIDS_STAT_COUNT);
+  stat_base_cpu = s[GIDS_STAT_CPU_ROWS];
+}
+
+void Store::print_stats() {
+  uint64_t s[GIDS_STAT_COUNT];
+  get_stats(s, GIDS_STAT_COUNT);
+  const double ms = kernel_time_ms();
+  const double hr = s[GIDS_STAT_ACCESS] ? (double)s[GIDS_STAT_HIT] / (double)s[GIDS_STAT_ACCESS] : 0.0;
+  printf("print stats: access %" PRIu64 " hit %" PRIu64 " miss %" PRIu64 " read_io %" PRIu64 " bypass %" PRIu64
+         " evictions %" PRIu64 " hit_rate %.4f\n",
+         s[GIDS_STAT_ACCESS], s[GIDS_STAT_HIT], s[GIDS_STAT_MISS], s[GIDS_STAT_READ_IO], s[GIDS_STAT_BYPASS],
+         s[GIDS_STAT_EVICTIONS], hr);
+  printf("cpu buffer rows: %" PRIu64 "  rows: %" PRIu64 "  wait timeouts: %" PRIu64 "  bad ids: %" PRIu64 "\n",
+         s[GIDS_STAT_CPU_ROWS], s[GIDS_STAT_ROWS], s[GIDS_STAT_WAIT_TIMEOUT], s[GIDS_STAT_BAD_IDS]);
+  printf("Kernel Time: \t %f\n", ms);
+  printf("Total Access: \t %" PRIu64 "\n", total_access);
+  fflush(stdout);
+  reset_stats();
+}
+
+}  // namespace gids

@@ -1,0 +1,212 @@
+/*
+ * gids_b200.h -- C ABI of the B200 GIDS feature-gather library (libgids_b200.so).
+ *
+ * The reference exposes this path to Python through the pybind11 module
+ * BAM_Feature_Store (gids_module/gids_nvme.cu:823-893), whose methods take raw
+ * uint64 device addresses. Every entry point below replaces one of those
+ * methods (or the host code behind it) and is cited next to its declaration.
+ * All entry points:
+ *   - take plain pointers and sizes (no torch or pybind types);
+ *   - return GIDS_OK (0) or a negative GIDS_E* code, with a message readable
+ *     through gids_last_error() on the calling thread;
+ *   - never abort the process.
+ * Streams are passed as `void*` holding a cudaStream_t (NULL = legacy default
+ * stream). Gathers are asynchronous on that stream unless the store is in
+ * synchronous mode (gids_store_set_synchronous), which is the default and
+ * matches the reference: the output is complete when the call returns.
+ *
+ * Element types: the store copies rows as bytes; elem_bytes is 2 (fp16/bf16),
+ * 4 (fp32, the reference's BAM_Feature_Store_float) or 8 (int64, the
+ * reference's BAM_Feature_Store_long).
+ */
+#ifndef GIDS_B200_H
+#define GIDS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GIDS_API __attribute__((visibility("default")))
+#else
+#define GIDS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ error codes */
+#define GIDS_OK 0
+#define GIDS_E_INVAL (-1)      /* bad argument (null pointer, size, alignment) */
+#define GIDS_E_CUDA (-2)       /* a CUDA runtime call failed */
+#define GIDS_E_NOMEM (-3)      /* host or device allocation failed */
+#define GIDS_E_STATE (-4)      /* call out of order (e.g. gather before init) */
+#define GIDS_E_RANGE (-5)      /* a node id addressed a row outside the store */
+#define GIDS_E_IO (-6)         /* emulated-SSD file could not be opened/mapped */
+#define GIDS_E_UNSUPPORTED (-7)
+
+#define GIDS_MAX_SSD 32
+#define GIDS_MAX_TUPLES 64
+
+typedef struct gids_ctrls gids_ctrls_t; /* emulated SSD controllers */
+typedef struct gids_store gids_store_t; /* one feature store (cache + CPU buffer) */
+
+/* Message of the last failed call on this thread (empty if none). Returns the
+ * message length. */
+GIDS_API int gids_last_error(char *buf, size_t len);
+GIDS_API const char *gids_strerror(int code);
+/* Library version string and the compiled GPU architecture. */
+GIDS_API const char *gids_version(void);
+/* The calling thread's current CUDA device (the reference hard-wires device
+ * 0, bam_nvme.h:135,293; a store here lives on the device it is created on). */
+GIDS_API int gids_current_device(int *out);
+
+/* --------------------------------------------------------- controllers --
+ * Replaces GIDS_Controllers::init_GIDS_controllers (gids_nvme.cu:93-107),
+ * which opens /dev/libnvm{ssd_list[i]} for i < n_ctrls with the given queue
+ * depth and queue count. Here each entry of ssd_list names an emulated SSD: a
+ * page-addressed region of host memory that the GPU reads zero-copy. q_depth
+ * and n_queues are recorded (there is no NVMe queue to size).
+ * If path_pattern is non-empty (gids_ctrls_set_emulation) the SSD of id k is
+ * the file path_pattern with "{}" replaced by k, mapped shared, so that its
+ * contents persist across processes like a device; otherwise it is anonymous
+ * memory owned by the process. */
+GIDS_API int gids_ctrls_create(gids_ctrls_t **out);
+GIDS_API int gids_ctrls_init(gids_ctrls_t *c, uint32_t n_ctrls, uint64_t q_depth, uint64_t n_queues, const int32_t *ssd_list);
+/* Emulation knobs (no reference counterpart; the reference's SSDs are real
+ * devices): capacity_bytes_per_ssd = 0 sizes each SSD to hold its stripe of
+ * the range; a smaller capacity makes the SSD wrap (logical page p is stored
+ * where page p mod (n_ctrls * data_pages_per_ssd) is). */
+GIDS_API int gids_ctrls_set_emulation(gids_ctrls_t *c, uint64_t capacity_bytes_per_ssd, const char *path_pattern);
+GIDS_API int gids_ctrls_destroy(gids_ctrls_t *c);
+
+/* --------------------------------------------------------------- store --
+ * Replaces BAM_Feature_Store<T>'s default constructor (gids_nvme.cu:812-815,
+ * pybind :830/:857) plus init_controllers (gids_nvme.cu:166-221):
+ *   page_size      bytes per cache page / SSD page (power of two, >= 512)
+ *   read_off_pages first page of the range on every SSD (GIDS.py:583 passes
+ *                  ceil(ceil(off / page_size) / num_ssd))
+ *   cache_size_mb  GPU page-cache size in MiB (n_slots = MiB * 2^20 / page_size)
+ *   num_ele        elements in the range (bounds of every gather)
+ *   num_ssd        SSDs the range is striped over (first num_ssd of ssd_list) */
+GIDS_API int gids_store_create(gids_store_t **out, uint32_t elem_bytes, int device);
+GIDS_API int gids_store_init_controllers(gids_store_t *s, gids_ctrls_t *c, uint32_t page_size, uint64_t read_off_pages,
+                                uint64_t cache_size_mb, uint64_t num_ele, uint64_t num_ssd);
+GIDS_API int gids_store_destroy(gids_store_t *s);
+/* 1 (default) = every gather synchronizes its stream before returning, like
+ * the reference (gids_nvme.cu:335,348); 0 = stream-ordered, asynchronous. */
+GIDS_API int gids_store_set_synchronous(gids_store_t *s, int synchronous);
+/* Source row stride (elements) used to fill the constant CPU buffer before
+ * the first gather tells it (the reference assumes one row per page,
+ * gids_nvme.cu:173,704). */
+GIDS_API int gids_store_set_row_layout(gids_store_t *s, uint32_t cache_dim);
+
+/* -------------------------------------------------------------- gathers --
+ * gids_read_feature replaces BAM_Feature_Store<T>::read_feature
+ * (gids_nvme.cu:324-364; kernels gids_kernel.cu:60-86 and :111-175):
+ *   out[i*dim + t] = range[(idx[i] + key_off) * cache_dim + t], t < dim,
+ * for i < n. `out` and `idx` are device pointers on the store's GPU; idx is
+ * int64. Rows pinned in the constant CPU buffer are read from it. A node id
+ * whose row leaves the range gives GIDS_E_RANGE and a zero row. */
+GIDS_API int gids_read_feature(gids_store_t *s, void *out, const int64_t *idx, int64_t n, int dim, int cache_dim,
+                      uint64_t key_off, void *stream);
+/* Replaces read_feature_hetero / read_feature_merged_hetero
+ * (gids_nvme.cu:382-445, :531-593) and, with key_offs == NULL,
+ * read_feature_merged (:456-518): k (out, idx, n, key_off) tuples gathered by
+ * ONE launch (the reference creates k streams and k launches). */
+GIDS_API int gids_read_feature_multi(gids_store_t *s, int k, void *const *outs, const int64_t *const *idxs,
+                            const uint64_t *ns, int dim, int cache_dim, const uint64_t *key_offs, void *stream);
+
+/* ---------------------------------------------------- window buffering --
+ * Replaces set_window_buffering (gids_nvme.cu:242-249; kernel
+ * gids_kernel.cu:246-256): marks the pages of the rows (idx[i] + hash_off)
+ * of an upcoming minibatch so that they are not evicted before that
+ * minibatch is gathered. Rows map to pages by bytes (the reference treats a
+ * node id as a page id). row_stride_elems = 0 uses the store's row layout. */
+GIDS_API int gids_set_window_buffering(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
+                              uint32_t row_stride_elems, void *stream);
+
+/* --------------------------------------------------- constant CPU buffer --
+ * cpu_backing_buffer (gids_nvme.cu:123-139): allocate a pinned, GPU-mapped
+ * host buffer of len rows x dim elements. Until set_cpu_buffer is called,
+ * rows [0, len) are the pinned set (the reference's seq mode,
+ * gids_kernel.cu:132-141). */
+GIDS_API int gids_cpu_backing_buffer(gids_store_t *s, uint64_t dim, uint64_t len);
+/* set_cpu_buffer (gids_nvme.cu:694-711; kernels gids_kernel.cu:191-228):
+ * pin the rows named by the first num entries of the int64 device array idx
+ * (a pin_file prefix) and fill the buffer from the backing store. */
+GIDS_API int gids_set_cpu_buffer(gids_store_t *s, const int64_t *idx, int num);
+/* Same, with a host array (no reference counterpart; used by host callers). */
+GIDS_API int gids_set_cpu_buffer_host(gids_store_t *s, const int64_t *idx, int64_t num);
+
+/* ---------------------------------------------------------- statistics --
+ * get_cpu_access_count / flush_cpu_access_count (gids_nvme.cu:779-794) and
+ * the page-cache counters printed by print_stats (gids_nvme.cu:261-300,
+ * page_cache_backup.h:974-977, 2046-2073). */
+GIDS_API int gids_get_cpu_access_count(gids_store_t *s, uint32_t *out);
+GIDS_API int gids_flush_cpu_access_count(gids_store_t *s);
+
+#define GIDS_STAT_ACCESS 0       /* page references (reference access_cnt) */
+#define GIDS_STAT_HIT 1          /* page references served by a resident page */
+#define GIDS_STAT_MISS 2         /* page references that waited for a fill */
+#define GIDS_STAT_READ_IO 3      /* pages filled from the backing store */
+#define GIDS_STAT_BYPASS 4       /* page references read straight from the backing store */
+#define GIDS_STAT_CPU_ROWS 5     /* rows served by the constant CPU buffer */
+#define GIDS_STAT_ROWS 6         /* rows gathered */
+#define GIDS_STAT_WAIT_TIMEOUT 7 /* bounded waits that gave up (then bypassed) */
+#define GIDS_STAT_BAD_IDS 8      /* node ids outside the range (zero rows) */
+#define GIDS_STAT_BYTES_HIT 9    /* output bytes copied from resident pages */
+#define GIDS_STAT_BYTES_MISS 10  /* output bytes copied from pages filled in this call */
+#define GIDS_STAT_BYTES_BYPASS 11
+#define GIDS_STAT_BYTES_CPU 12
+#define GIDS_STAT_EVICTIONS 13
+#define GIDS_STAT_LAUNCHES 14    /* gather kernels launched */
+#define GIDS_STAT_COUNT 16
+/* Copies the cumulative counters (synchronizes the store's last stream). */
+GIDS_API int gids_get_stats(gids_store_t *s, uint64_t *out, int count);
+GIDS_API int gids_reset_stats(gids_store_t *s);
+/* print_stats (gids_nvme.cu:279-300): prints and resets the counters and the
+ * accumulated gather time. */
+GIDS_API int gids_print_stats(gids_store_t *s);
+/* Accumulated device time of gathers since the last print/reset, in ms. */
+GIDS_API int gids_get_kernel_time_ms(gids_store_t *s, double *out);
+GIDS_API int gids_store_synchronize(gids_store_t *s);
+
+/* ------------------------------------------------------- backing store --
+ * store_tensor (gids_nvme.cu:616-663; kernel gids_kernel.cu:378-389): row r
+ * < num_rows of the range, one page of elements (page_size / elem_bytes) per
+ * row as in the reference (gids_nvme.cu:173), receives the elements that
+ * start offset_bytes / elem_bytes elements into `src` (device or host
+ * pointer) -- the reference applies the offset to the source and always
+ * writes from element 0 of the range. The write goes through the stripe map
+ * to the emulated SSDs; resident copies are then dropped so that gathers see
+ * the new data (the reference flushes its dirty pages, flush_cache,
+ * gids_nvme.cu:673-677). */
+GIDS_API int gids_store_tensor(gids_store_t *s, const void *src, uint64_t num_rows, uint64_t offset_bytes);
+/* General striped writer: nbytes from src (device or host pointer) to the
+ * range at byte offset_bytes; resident copies are dropped. No reference
+ * counterpart (the reference writes whole pages from row 0 only). */
+GIDS_API int gids_write_range(gids_store_t *s, const void *src, uint64_t nbytes, uint64_t offset_bytes);
+/* flush_cache (gids_nvme.cu:673-677): the cache holds no dirty pages here,
+ * so this drops every resident page. */
+GIDS_API int gids_flush_cache(gids_store_t *s);
+/* Host-side read of the range through the stripe map (no reference
+ * counterpart; the reference's read_tensor prints elements from a GPU
+ * thread, gids_nvme.cu:764-770). */
+GIDS_API int gids_read_range_host(gids_store_t *s, void *dst, uint64_t nbytes, uint64_t offset_bytes);
+/* Fill the whole backing store with the synthetic feature stream `kind`
+ * (1 = fp32 uniform[-1,1), 2 = fp16 byte-sum, 3 = int64 raw) of `seed`:
+ * element e of the range holds element (e mod wrap) of the stream, where
+ * wrap covers the pages the SSDs physically hold. Uses `threads` host threads
+ * (0 = all). No reference counterpart: the reference's SSDs are filled by
+ * tensor_write.py / nvm-readwrite_stripe-bench before training. */
+GIDS_API int gids_fill_synthetic(gids_store_t *s, int kind, uint64_t seed, int threads);
+/* Geometry of the bound backing store: [0]=pages in the range, [1]=pages
+ * physically held (wrap period), [2]=bytes per SSD, [3]=cache slots,
+ * [4]=page size, [5]=number of SSDs. */
+GIDS_API int gids_store_geometry(gids_store_t *s, uint64_t *out, int count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GIDS_B200_H */
