@@ -23,9 +23,12 @@ A config-2 step reads about 13 GB, far larger than the 126 MB L2, so no
 flush is needed between steps (the line's config.l2 states the size).
 
 Multi-GPU (torchrun): one process per GPU, each an independent
-data-parallel trainer with its own sampler seed (1000 + rank) and its own
-page cache; the emulated SSDs are one shared-memory copy mapped by every
-rank. NCCL only carries barriers and the max-over-ranks timing.
+data-parallel trainer with its own sampler seed (1000 + rank). The ranks'
+page caches form one cache sharded by page id (page p on rank p % N; hits on
+other ranks' pages are NVLink peer loads, misses fill the owner's slot);
+the emulated SSDs are one shared-memory copy mapped by every rank. Only
+setup (CUDA IPC handles), barriers and the max-over-ranks timing use
+torch.distributed.
 """
 from __future__ import annotations
 
@@ -278,19 +281,30 @@ def run_ours(args, cfg, dist: Dist):
     pattern = f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd{{}}" if shared else None
 
     t0 = time.time()
-    if shared and dist.rank != 0:
-        dist.barrier()  # rank 0 creates and fills the shared emulated SSDs first
+    t_fill = 0.0
+    if shared:
+        # rank 0 writes the shared emulated SSDs once; every rank then maps them
+        if dist.rank == 0:
+            import BAM_Feature_Store
+
+            c = BAM_Feature_Store.GIDS_Controllers()
+            c.init_GIDS_controllers(cfg["ssds"], 1024, 128, list(range(cfg["ssds"])))
+            c.set_emulation(per_ssd if phys < range_bytes else 0, pattern)
+            c.bind(cfg["ssds"], page, 0, range_bytes)
+            tf = time.time()
+            c.fill_synthetic(KIND[dt], 1, 0)
+            t_fill = time.time() - tf
+            del c
+        dist.barrier()
     g = GIDS.GIDS(page_size=page, off=0, cache_dim=dim, num_ele=num_ele, num_ssd=cfg["ssds"],
                   ssd_list=list(range(cfg["ssds"])), cache_size=cfg["cache_mb"], ctrl_idx=dist.local,
                   dtype=TDTYPE[dt], ssd_capacity=per_ssd if phys < range_bytes else 0, ssd_path=pattern,
-                  synchronous=False)
+                  synchronous=False, shard_cache=shared and not args.no_shard)
     t_store = time.time() - t0
-    t0 = time.time()
-    if not shared or dist.rank == 0:
+    if not shared:
+        t0 = time.time()
         g.BAM_FS.fill_synthetic(KIND[dt], 1, 0)
-    t_fill = time.time() - t0
-    if shared and dist.rank == 0:
-        dist.barrier()
+        t_fill = time.time() - t0
     geo = g.BAM_FS.geometry()
     log(f"[rank {dist.rank}] store ready: {geo} (alloc {t_store:.1f}s, fill {t_fill:.1f}s)")
 
@@ -324,10 +338,12 @@ def run_ours(args, cfg, dist: Dist):
     dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("gids_timed_value")
     ev0.record(stream)
     for ids in dev_ids:
         gather_dev(ids)
     ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     dist.barrier()
     t_val = ev0.elapsed_time(ev1) / 1e3
@@ -345,12 +361,14 @@ def run_ours(args, cfg, dist: Dist):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
+    torch.cuda.nvtx.range_push("gids_timed_e2e")
     e0.record(stream)
     checks = 0.0
     for _ in e2e_batches:
         batch = g.fetch_feature(dim, it, device)
         checks += float(batch[-1][-1, -1].item())  # D2H read of the step's result
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     wall_e2e = time.perf_counter() - w0
     dist.barrier()
@@ -391,7 +409,8 @@ def run_ours(args, cfg, dist: Dist):
         "host_link": {"alg_bytes_per_launch": int(r_host), "achieved_gbs": round(r_host / t_launch / 1e9, 2),
                       "peak_gbs": round(host_peak, 2)},
         "mix": {"hit": round(st["hit"] / acc, 4), "miss": round(st["miss"] / acc, 4),
-                "bypass": round(st["bypass"] / acc, 4), "cpu_rows": st["cpu_rows"]},
+                "bypass": round(st["bypass"] / acc, 4), "cpu_rows": st["cpu_rows"],
+                "peer_bytes_frac": round(st.get("bytes_peer", 0) / max(1, st["rows"] * row_bytes), 4)},
     }
     gb_val = rows_val_all * row_bytes / 1e9
     value = gb_val / t_val_max
@@ -406,7 +425,9 @@ def run_ours(args, cfg, dist: Dist):
         "config": {"workload": f"{args.config}: {cfg['nodes']} nodes, {dt} x {dim} ({range_bytes / 1e9:.1f} GB range), "
                                f"{page} B pages over {cfg['ssds']} emulated SSDs, {cfg['cache_mb'] // 1024} GB cache/GPU, "
                                f"fanout {cfg['fanouts']}, batch {cfg['batch']}",
-                   "global_batch": cfg["batch"] * dist.world, "parallelism": f"dp{dist.world} (independent trainers)",
+                   "global_batch": cfg["batch"] * dist.world,
+                   "parallelism": f"dp{dist.world} (independent trainers" +
+                                  (", page cache sharded by page id over NVLink)" if g.world > 1 else ")"),
                    "backing_store": {"logical_bytes": range_bytes, "physical_bytes": geo["wrap_pages"] * page,
                                      "wrap_pages": geo["wrap_pages"]},
                    "l2": (f"no flush: every step reads {min(sizes) * row_bytes / 1e9:.2f} GB or more (L2 is 126 MB)"
@@ -468,6 +489,7 @@ def main():
     ap.add_argument("--cache-mb", type=int, default=0, help="override the cache size")
     ap.add_argument("--batch", type=int, default=0, help="override the seed batch size (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--no-shard", action="store_true", help="N>1: independent caches instead of one sharded cache")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3")

@@ -64,14 +64,18 @@ class GIDS:
     extensions: ``dtype`` (feature element type; default float32, int64 with
     ``long_type``), ``ssd_capacity`` (bytes held per emulated SSD, 0 = the
     whole stripe; smaller values wrap), ``ssd_path`` (file pattern such as
-    ``/dev/shm/gids_ssd{}`` for emulated SSDs shared across processes) and
-    ``synchronous``.
+    ``/dev/shm/gids_ssd{}`` for emulated SSDs shared across processes),
+    ``synchronous``, and ``shard_cache``: with torch.distributed initialised
+    (one process per GPU), the ranks' page caches form one cache sharded by
+    page id (page p lives on rank p % world) and hits on other ranks' pages
+    are read over NVLink. Every rank must construct its GIDS collectively
+    with the same geometry, and call ``close()`` collectively.
     """
 
     def __init__(self, page_size=4096, off=0, cache_dim=1024, num_ele=300 * 1000 * 1000 * 1024, num_ssd=1,
                  ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
                  long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
-                 ssd_path=None, synchronous=False):
+                 ssd_path=None, synchronous=False, shard_cache=False, process_group=None):
         if dtype is None:
             dtype = torch.int64 if long_type else torch.float32
         if dtype not in _STORE_CLASSES:
@@ -114,13 +118,47 @@ class GIDS:
             self.GIDS_controller.set_emulation(int(ssd_capacity or 0), ssd_path or "")
 
         self.BAM_FS.set_device(ctrl_idx)
+        self._pg = None
+        self.world, self.rank = 1, 0
+        if shard_cache:
+            import torch.distributed as dist
+
+            if dist.is_available() and dist.is_initialized():
+                self._pg = process_group
+                self.world = dist.get_world_size(process_group)
+                self.rank = dist.get_rank(process_group)
+            if self.world > 1:
+                self.BAM_FS.set_sharding(self.world, self.rank)
         self.BAM_FS.init_controllers(self.GIDS_controller, page_size, self.off, cache_size, num_ele, num_ssd)
+        if self.world > 1:
+            self._attach_peer_shards()
         self.BAM_FS.set_row_layout(cache_dim)
         self.BAM_FS.set_synchronous(bool(synchronous))
         self.synchronous = bool(synchronous)
 
         self.GIDS_time = 0.0
         self.WB_time = 0.0
+
+    def _attach_peer_shards(self):
+        """Exchange the shards' CUDA IPC handles and map every peer's shard."""
+        import torch.distributed as dist
+
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.BAM_FS.ipc_handle(), group=self._pg)
+        self.BAM_FS.open_peers(handles)
+        dist.barrier(group=self._pg)
+
+    def close(self):
+        """Release the store. With a sharded cache this is collective: no rank
+        frees its shard while another may still read it."""
+        if getattr(self, "BAM_FS", None) is None:
+            return
+        self.BAM_FS.synchronize()
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(group=self._pg)
+        self.BAM_FS = None
 
     # ------------------------------------------------------------ out of scope
     def init_graph_GIDS(self, page_size, off, cache_size, num_ele, num_ssd):

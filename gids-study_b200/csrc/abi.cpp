@@ -109,6 +109,57 @@ int gids_ctrls_destroy(gids_ctrls_t* c) {
   return guarded([&] { delete c; });
 }
 
+int gids_ctrls_bind(gids_ctrls_t* c, uint32_t num_ssd, uint32_t page_size, uint64_t read_off_pages,
+                    uint64_t range_bytes) {
+  return guarded([&] {
+    NEED(c);
+    GIDS_CHECK(page_size >= 512 && (page_size & (page_size - 1)) == 0, GIDS_E_INVAL,
+               "page_size must be a power of two >= 512");
+    GIDS_CHECK(num_ssd >= 1 && num_ssd <= c->c.n_ctrls, GIDS_E_INVAL, "num_ssd must be in [1, controllers]");
+    GIDS_CHECK(range_bytes > 0, GIDS_E_INVAL, "empty range");
+    c->c.bind(num_ssd, page_size, read_off_pages, (range_bytes + page_size - 1) / page_size);
+  });
+}
+
+int gids_ctrls_write(gids_ctrls_t* c, const void* src, uint64_t nbytes, uint64_t off) {
+  return guarded([&] {
+    NEED(c);
+    GIDS_CHECK(c->c.bound, GIDS_E_STATE, "controllers not bound");
+    GIDS_CHECK(off + nbytes <= c->c.range_pages * c->c.page_size, GIDS_E_RANGE, "write past the end of the range");
+    if (nbytes) NEED(src);
+    gids::backing_write(c->c, src, nbytes, off);
+  });
+}
+
+int gids_ctrls_read(gids_ctrls_t* c, void* dst, uint64_t nbytes, uint64_t off) {
+  return guarded([&] {
+    NEED(c);
+    GIDS_CHECK(c->c.bound, GIDS_E_STATE, "controllers not bound");
+    GIDS_CHECK(off + nbytes <= c->c.range_pages * c->c.page_size, GIDS_E_RANGE, "read past the end of the range");
+    if (nbytes) NEED(dst);
+    gids::backing_read(c->c, dst, nbytes, off);
+  });
+}
+
+int gids_ctrls_fill_synthetic(gids_ctrls_t* c, int kind, uint64_t seed, int threads) {
+  return guarded([&] {
+    NEED(c);
+    GIDS_CHECK(c->c.bound, GIDS_E_STATE, "controllers not bound");
+    gids::backing_fill_synthetic(c->c, kind, seed, threads);
+  });
+}
+
+int gids_ctrls_geometry(gids_ctrls_t* c, uint64_t* out, int count) {
+  return guarded([&] {
+    NEED(c);
+    NEED(out);
+    GIDS_CHECK(c->c.bound, GIDS_E_STATE, "controllers not bound");
+    const uint64_t g[4] = {c->c.range_pages, c->c.wrap_pages, c->c.ssd.empty() ? 0 : c->c.ssd[0].bytes,
+                           c->c.n_bound};
+    for (int i = 0; i < count && i < 4; i++) out[i] = g[i];
+  });
+}
+
 int gids_store_create(gids_store_t** out, uint32_t elem_bytes, int device) {
   return guarded([&] {
     NEED(out);
@@ -140,6 +191,45 @@ int gids_store_set_row_layout(gids_store_t* s, uint32_t cache_dim) {
   return guarded([&] {
     NEED(s);
     s->s.set_row_layout(cache_dim);
+  });
+}
+
+int gids_store_set_sharding(gids_store_t* s, int world, int rank) {
+  return guarded([&] {
+    NEED(s);
+    GIDS_CHECK(world >= 1 && rank >= 0, GIDS_E_INVAL, "bad world/rank");
+    s->s.set_sharding((uint32_t)world, (uint32_t)rank);
+  });
+}
+
+int gids_store_ipc_handle(gids_store_t* s, void* out, size_t len) {
+  return guarded([&] {
+    NEED(s);
+    NEED(out);
+    GIDS_CHECK(len >= sizeof(cudaIpcMemHandle_t), GIDS_E_INVAL, "handle buffer must hold 64 bytes");
+    s->s.ipc_handle(out);
+  });
+}
+
+int gids_store_open_peers(gids_store_t* s, const void* handles, int world) {
+  return guarded([&] {
+    NEED(s);
+    NEED(handles);
+    GIDS_CHECK(world >= 1, GIDS_E_INVAL, "bad world");
+    s->s.open_peers(handles, (uint32_t)world);
+  });
+}
+
+int gids_store_share_shards(gids_store_t* const* stores, int n) {
+  return guarded([&] {
+    NEED(stores);
+    GIDS_CHECK(n >= 1 && n <= GIDS_MAX_WORLD, GIDS_E_INVAL, "1..8 stores");
+    std::vector<gids::Store*> v;
+    for (int i = 0; i < n; i++) {
+      GIDS_CHECK(stores[i] != nullptr, GIDS_E_INVAL, "null store");
+      v.push_back(&stores[i]->s);
+    }
+    gids::Store::share_in_process(v.data(), (uint32_t)n);
   });
 }
 

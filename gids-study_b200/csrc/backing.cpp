@@ -129,7 +129,11 @@ void Controllers::set_emulation(uint64_t cap, const char* pat) {
 }
 
 uint64_t Controllers::bind(uint32_t n, uint32_t ps, uint64_t start, uint64_t pages) {
-  GIDS_CHECK(!bound, GIDS_E_STATE, "controllers already bound to a store");
+  if (bound) {  // reuse a binding made with the same geometry
+    GIDS_CHECK(n == n_bound && ps == page_size && start == page_start && pages == range_pages, GIDS_E_STATE,
+               "controllers already bound with a different geometry");
+    return wrap_pages;
+  }
   GIDS_CHECK(n_ctrls >= n, GIDS_E_STATE, "init_GIDS_controllers first");
   page_size = ps;
   page_start = start;

@@ -46,6 +46,23 @@ struct Controllers {
   void set_emulation(uint64_t capacity, const std::string& pattern) {
     check(gids_ctrls_set_emulation(c, capacity, pattern.c_str()));
   }
+  // extension: the backing store without a GPU cache
+  void bind(uint32_t num_ssd, uint32_t page_size, uint64_t read_off_pages, uint64_t range_bytes) {
+    check(gids_ctrls_bind(c, num_ssd, page_size, read_off_pages, range_bytes));
+  }
+  void write(uint64_t src, uint64_t nbytes, uint64_t off) { check(gids_ctrls_write(c, (const void*)src, nbytes, off)); }
+  void read_into(uint64_t dst, uint64_t nbytes, uint64_t off) { check(gids_ctrls_read(c, (void*)dst, nbytes, off)); }
+  void fill_synthetic(int kind, uint64_t seed, int threads) { check(gids_ctrls_fill_synthetic(c, kind, seed, threads)); }
+  py::dict geometry() {
+    uint64_t g[4] = {0};
+    check(gids_ctrls_geometry(c, g, 4));
+    py::dict d;
+    d["range_pages"] = g[0];
+    d["wrap_pages"] = g[1];
+    d["ssd_bytes"] = g[2];
+    d["num_ssd"] = g[3];
+    return d;
+  }
 };
 
 class FeatureStore {
@@ -73,7 +90,9 @@ class FeatureStore {
     if (dev < 0) check(gids_current_device(&dev));
     gids_store_t* s = nullptr;
     check(gids_store_create(&s, eb_, dev));
-    int rc = gids_store_init_controllers(s, ctrl.c, ps, read_off, cache_size, num_ele, num_ssd);
+    int rc = GIDS_OK;
+    if (world_ > 1) rc = gids_store_set_sharding(s, world_, rank_);
+    if (rc == GIDS_OK) rc = gids_store_init_controllers(s, ctrl.c, ps, read_off, cache_size, num_ele, num_ssd);
     if (rc != GIDS_OK) {
       char buf[1024];
       gids_last_error(buf, sizeof(buf));
@@ -155,6 +174,26 @@ class FeatureStore {
   uint64_t get_offset_array() { return (uint64_t)(uintptr_t)offsets_.data(); }
 
   // ---- extensions
+  // sharded cache (must be set before init_controllers)
+  void set_sharding(int world, int rank) {
+    if (s_) throw std::runtime_error("gids: set_sharding after init_controllers");
+    world_ = world;
+    rank_ = rank;
+  }
+  py::bytes ipc_handle() {
+    char h[64];
+    check(gids_store_ipc_handle(s(), h, sizeof(h)));
+    return py::bytes(h, sizeof(h));
+  }
+  void open_peers(const std::vector<std::string>& handles) {
+    std::string all;
+    for (const auto& h : handles) {
+      if (h.size() != 64) throw std::runtime_error("gids: IPC handles are 64 bytes");
+      all += h;
+    }
+    py::gil_scoped_release r;
+    check(gids_store_open_peers(s(), all.data(), (int)handles.size()));
+  }
   void set_synchronous(bool v) { check(gids_store_set_synchronous(s(), v ? 1 : 0)); }
   void set_row_layout(uint32_t cache_dim) { check(gids_store_set_row_layout(s(), cache_dim)); }
   void synchronize() { check(gids_store_synchronize(s())); }
@@ -167,8 +206,9 @@ class FeatureStore {
     py::dict d;
     static const char* names[] = {"access",      "hit",       "miss",          "read_io",     "bypass",
                                   "cpu_rows",    "rows",      "wait_timeouts", "bad_ids",     "bytes_hit",
-                                  "bytes_miss",  "bytes_bypass", "bytes_cpu",   "evictions",   "launches"};
-    for (int i = 0; i < 15; i++) d[names[i]] = v[i];
+                                  "bytes_miss",  "bytes_bypass", "bytes_cpu",   "evictions",   "launches",
+                                  "bytes_peer"};
+    for (int i = 0; i < 16; i++) d[names[i]] = v[i];
     return d;
   }
   void reset_stats() { check(gids_reset_stats(s())); }
@@ -207,6 +247,7 @@ class FeatureStore {
   }
   uint32_t eb_;
   int device_ = -1;
+  int world_ = 1, rank_ = 0;
   uint32_t page_size_ = 0;
   gids_store_t* s_ = nullptr;
   std::vector<uint64_t> offsets_{0, 0, 0};
@@ -256,6 +297,9 @@ void bind_store(py::module_& m, const char* name) {
       .def("print_stats", &S::print_stats, R())
       // extensions
       .def("set_device", &S::set_device)
+      .def("set_sharding", &S::set_sharding, py::arg("world"), py::arg("rank"))
+      .def("ipc_handle", &S::ipc_handle)
+      .def("open_peers", &S::open_peers)
       .def("set_synchronous", &S::set_synchronous, R())
       .def("set_row_layout", &S::set_row_layout, R())
       .def("synchronize", &S::synchronize, R())
@@ -280,10 +324,24 @@ PYBIND11_MODULE(BAM_Feature_Store, m) {
            py::arg("ssd_list"))
       .def("set_emulation", &Controllers::set_emulation, py::arg("capacity_bytes_per_ssd") = 0,
            py::arg("path_pattern") = std::string())
+      .def("bind", &Controllers::bind, py::arg("num_ssd"), py::arg("page_size"), py::arg("read_off_pages"),
+           py::arg("range_bytes"), py::call_guard<py::gil_scoped_release>())
+      .def("write", &Controllers::write, py::call_guard<py::gil_scoped_release>())
+      .def("read_into", &Controllers::read_into, py::call_guard<py::gil_scoped_release>())
+      .def("fill_synthetic", &Controllers::fill_synthetic, py::arg("kind"), py::arg("seed"), py::arg("threads") = 0,
+           py::call_guard<py::gil_scoped_release>())
+      .def("geometry", &Controllers::geometry)
       .def_readonly("n_ctrls", &Controllers::n_ctrls);
   bind_store<4, 0>(m, "BAM_Feature_Store_float");
   bind_store<8, 0>(m, "BAM_Feature_Store_long");
   bind_store<2, 0>(m, "BAM_Feature_Store_half");
   bind_store<2, 1>(m, "BAM_Feature_Store_bfloat16");
   m.def("version", []() { return std::string(gids_version()); });
+  // extension: one process driving every GPU of a sharded cache
+  m.def("share_shards", [](py::list stores) {
+    std::vector<gids_store_t*> v;
+    for (auto h : stores) v.push_back((gids_store_t*)(uintptr_t)h.attr("handle").cast<uint64_t>());
+    py::gil_scoped_release r;
+    check(gids_store_share_shards(v.data(), (int)v.size()));
+  });
 }

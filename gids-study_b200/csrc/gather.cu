@@ -36,39 +36,106 @@
 namespace gids {
 namespace {
 
-// ------------------------------------------------------------ atomics (gpu scope)
+// ------------------------------------------------------------ scoped atomics
+// SYS = false: the cache is private to this GPU (gpu scope).
+// SYS = true:  shards live on several GPUs and are read and filled over
+//              NVLink, so every state-word operation uses system scope.
+template <bool SYS>
 __device__ __forceinline__ unsigned long long atom_add_acquire(unsigned long long* p, unsigned long long v) {
   unsigned long long r;
-  asm volatile("atom.acquire.gpu.global.add.u64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  if (SYS)
+    asm volatile("atom.acquire.sys.global.add.u64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  else
+    asm volatile("atom.acquire.gpu.global.add.u64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
   return r;
 }
+template <bool SYS>
 __device__ __forceinline__ unsigned long long atom_or_acquire(unsigned long long* p, unsigned long long v) {
   unsigned long long r;
-  asm volatile("atom.acquire.gpu.global.or.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  if (SYS)
+    asm volatile("atom.acquire.sys.global.or.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  else
+    asm volatile("atom.acquire.gpu.global.or.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
   return r;
 }
-__device__ __forceinline__ unsigned long long atom_and_relaxed(unsigned long long* p, unsigned long long v) {
+template <bool SYS>
+__device__ __forceinline__ void atom_and_relaxed(unsigned long long* p, unsigned long long v) {
   unsigned long long r;
-  asm volatile("atom.relaxed.gpu.global.and.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  if (SYS)
+    asm volatile("atom.relaxed.sys.global.and.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  else
+    asm volatile("atom.relaxed.gpu.global.and.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  (void)r;
+}
+template <bool SYS>
+__device__ __forceinline__ void red_add_release(unsigned long long* p, unsigned long long v) {
+  if (SYS)
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+  else
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+template <bool SYS>
+__device__ __forceinline__ unsigned long long atom_add_relaxed(unsigned long long* p, unsigned long long v) {
+  unsigned long long r;
+  if (SYS)
+    asm volatile("atom.relaxed.sys.global.add.u64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  else
+    asm volatile("atom.relaxed.gpu.global.add.u64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
   return r;
 }
-__device__ __forceinline__ void red_add_release(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
+template <bool SYS>
 __device__ __forceinline__ unsigned long long atom_cas_acq_rel(unsigned long long* p, unsigned long long cmp,
                                                                unsigned long long val) {
   unsigned long long r;
-  asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;" : "=l"(r) : "l"(p), "l"(cmp), "l"(val) : "memory");
+  if (SYS)
+    asm volatile("atom.acq_rel.sys.global.cas.b64 %0, [%1], %2, %3;" : "=l"(r) : "l"(p), "l"(cmp), "l"(val) : "memory");
+  else
+    asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;" : "=l"(r) : "l"(p), "l"(cmp), "l"(val) : "memory");
   return r;
 }
+template <bool SYS>
+__device__ __forceinline__ unsigned long long atom_exch_relaxed(unsigned long long* p, unsigned long long v) {
+  unsigned long long r;
+  if (SYS)
+    asm volatile("atom.relaxed.sys.global.exch.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  else
+    asm volatile("atom.relaxed.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  return r;
+}
+template <bool SYS>
 __device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
   unsigned long long r;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  if (SYS)
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  else
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
   return r;
 }
+template <bool SYS>
 __device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
   unsigned long long r;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  if (SYS)
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  return r;
+}
+template <bool SYS>
+__device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int* p) {
+  unsigned int r;
+  if (SYS)
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+  return r;
+}
+template <bool SYS>
+__device__ __forceinline__ unsigned int atom_cas_u32(unsigned int* p, unsigned int cmp, unsigned int val) {
+  unsigned int r;
+  if (SYS)
+    asm volatile("atom.relaxed.sys.global.cas.b32 %0, [%1], %2, %3;" : "=r"(r) : "l"(p), "r"(cmp), "r"(val) : "memory");
+  else
+    asm volatile("atom.relaxed.gpu.global.cas.b32 %0, [%1], %2, %3;" : "=r"(r) : "l"(p), "r"(cmp), "r"(val) : "memory");
   return r;
 }
 
@@ -168,23 +235,28 @@ __device__ __forceinline__ const char* backing_addr(const DevBacking& b, uint64_
 }
 
 // Saturating decrement of a window-buffer pin counter (bounded CAS loop).
+template <bool SYS>
 __device__ __forceinline__ void wb_consume(unsigned int* w, unsigned int cnt) {
-  unsigned int v = *reinterpret_cast<volatile unsigned int*>(w);
+  unsigned int v = ld_relaxed_u32<SYS>(w);
   for (int it = 0; v != 0 && it < 64; it++) {
     const unsigned int nv = v > cnt ? v - cnt : 0u;
-    const unsigned int r = atomicCAS(w, v, nv);
+    const unsigned int r = atom_cas_u32<SYS>(w, v, nv);
     if (r == v) break;
     v = r;
   }
 }
 
-enum { K_ROWS, K_CPU, K_BAD, K_ACCESS, K_HIT, K_MISS, K_BYPASS, K_READIO, K_TIMEOUT, K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_N };
-__constant__ int kStatMap[K_N] = {GIDS_STAT_ROWS,       GIDS_STAT_CPU_ROWS,   GIDS_STAT_BAD_IDS,    GIDS_STAT_ACCESS,
-                                  GIDS_STAT_HIT,        GIDS_STAT_MISS,       GIDS_STAT_BYPASS,     GIDS_STAT_READ_IO,
-                                  GIDS_STAT_WAIT_TIMEOUT, GIDS_STAT_BYTES_HIT, GIDS_STAT_BYTES_MISS, GIDS_STAT_BYTES_BYPASS,
-                                  GIDS_STAT_BYTES_CPU,  GIDS_STAT_EVICTIONS};
+enum {
+  K_ROWS, K_CPU, K_BAD, K_ACCESS, K_HIT, K_MISS, K_BYPASS, K_READIO, K_TIMEOUT,
+  K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_BPEER, K_N
+};
+__constant__ int kStatMap[K_N] = {GIDS_STAT_ROWS,       GIDS_STAT_CPU_ROWS,     GIDS_STAT_BAD_IDS,
+                                  GIDS_STAT_ACCESS,     GIDS_STAT_HIT,          GIDS_STAT_MISS,
+                                  GIDS_STAT_BYPASS,     GIDS_STAT_READ_IO,      GIDS_STAT_WAIT_TIMEOUT,
+                                  GIDS_STAT_BYTES_HIT,  GIDS_STAT_BYTES_MISS,   GIDS_STAT_BYTES_BYPASS,
+                                  GIDS_STAT_BYTES_CPU,  GIDS_STAT_EVICTIONS,    GIDS_STAT_BYTES_PEER};
 
-template <int VEC>
+template <int VEC, bool SYS>
 __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_constant__ GatherArgs a) {
   __shared__ SegDesc seg_sh[WARPS][32];
   __shared__ unsigned long long cnt_sh[WARPS][K_N];  // warp-private counters
@@ -200,6 +272,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
   const uint32_t shift = a.c.page_shift;
   const uint64_t psize = a.c.page_size;
   const bool have_cache = a.c.n_slots != 0;
+  const uint32_t world = a.c.world;
   const uint64_t n_warps = (uint64_t)gridDim.x * WARPS;
 
   int ti = 0;
@@ -232,7 +305,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       }
     }
 
-    // ---- page segment of this lane
+    // ---- page segment of this lane, and the shard that owns the page
     const uint64_t b0 = r * a.src_stride;
     const uint64_t p_first = b0 >> shift;
     const uint64_t p_last = (b0 + a.row_bytes - 1) >> shift;
@@ -245,6 +318,9 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       const uint64_t pe = pb + psize, re = b0 + a.row_bytes;
       s1 = (uint32_t)((pe < re ? pe : re) - b0);
     }
+    const uint32_t owner = (SYS && seg_ok) ? (uint32_t)(p % world) : 0u;
+    const uint64_t lp = SYS ? p / world : p;  // index in the owner's page table
+    const DevShard& S = a.c.sh[owner];
 
     // ---- 2. warp dedup + acquire (one leader per distinct page)
     const unsigned long long key = seg_ok ? (unsigned long long)p : (~0ull - (unsigned long long)lane);
@@ -254,20 +330,20 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const unsigned cnt = __popc(eq);
     int cls = CLS_NONE;
     uint64_t slot = 0;
-    unsigned long long* stw = a.c.state + (seg_ok ? p : 0);
+    unsigned long long* stw = S.state + (seg_ok ? lp : 0);
     const bool took_ref = is_leader && have_cache;
     if (is_leader) {
       if (!have_cache) {
         cls = CLS_BYPASS;
       } else {
-        const unsigned long long old = atom_add_acquire(stw, cnt);
+        const unsigned long long old = atom_add_acquire<SYS>(stw, cnt);
         if (old & ST_VALID) {
           cls = CLS_HIT;
           slot = old >> ST_SLOT_SHIFT;
         } else if (old & ST_BUSY) {
           cls = CLS_WAIT;
         } else {
-          const unsigned long long prev = atom_or_acquire(stw, ST_BUSY);
+          const unsigned long long prev = atom_or_acquire<SYS>(stw, ST_BUSY);
           if (prev & ST_VALID) {
             cls = CLS_HIT;
             slot = prev >> ST_SLOT_SHIFT;
@@ -280,55 +356,65 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       }
     }
 
-    // ---- 3. fills: warp-cooperative clock sweep for victim slots, then copies
+    // ---- 3. fills: per owning shard, a warp-cooperative clock sweep for
+    //         victim slots (32 candidates per atomic on that shard's hand)
     unsigned pending = __ballot_sync(0xffffffffu, cls == CLS_OWN);
     if (pending) {
-      for (uint32_t round = 0; pending && round < a.sweep_limit; round++) {
-        unsigned long long base = 0;
-        if (lane == 0) base = atomicAdd(a.c.clock, 32ull);
-        base = __shfl_sync(0xffffffffu, base, 0);
-        const uint64_t s = (base + (uint64_t)lane) % a.c.n_slots;
-        const unsigned long long q = ld_relaxed(a.c.slot_page + s);
-        bool cand = false;
-        unsigned long long expect = 0;
-        if (q == SLOT_EMPTY) {
-          cand = true;
-        } else if (a.c.slot_ref[s]) {
-          a.c.slot_ref[s] = 0;  // second chance
-        } else {
-          const unsigned long long st = ld_relaxed(a.c.state + q);
-          if (st == (((unsigned long long)s << ST_SLOT_SHIFT) | ST_VALID) && (!a.c.wb || a.c.wb[q] == 0)) {
+      unsigned todo = pending;
+      while (todo) {
+        const uint32_t tgt = __shfl_sync(0xffffffffu, owner, __ffs(todo) - 1);
+        unsigned grp = todo & __ballot_sync(0xffffffffu, owner == tgt);
+        todo &= ~grp;
+        const DevShard& V = a.c.sh[tgt];
+        for (uint32_t round = 0; grp && round < a.sweep_limit; round++) {
+          unsigned long long base = 0;
+          if (lane == 0) base = atom_add_relaxed<SYS>(V.clock, 32ull);
+          base = __shfl_sync(0xffffffffu, base, 0);
+          const uint64_t s = (base + (uint64_t)lane) % a.c.n_slots;
+          const unsigned long long q = ld_relaxed<SYS>(V.slot_page + s);
+          bool cand = false;
+          unsigned long long expect = 0;
+          if (q == SLOT_EMPTY) {
             cand = true;
-            expect = st;
-          }
-        }
-        unsigned cmask = __ballot_sync(0xffffffffu, cand);
-        while (cmask && pending) {
-          const int c = __ffs(cmask) - 1;
-          cmask &= cmask - 1;
-          const int o = __ffs(pending) - 1;
-          const unsigned long long newp = __shfl_sync(0xffffffffu, (unsigned long long)p, o);
-          int ok = 0;
-          if (lane == c) {
-            if (q == SLOT_EMPTY) {
-              ok = atom_cas_acq_rel(a.c.slot_page + s, SLOT_EMPTY, newp) == SLOT_EMPTY;
-            } else if (atom_cas_acq_rel(a.c.state + q, expect, 0ull) == expect) {
-              atomicExch(a.c.slot_page + s, newp);
-              atomicAdd(acc + K_EVICT, 1ull);
-              ok = 1;
+          } else if (V.slot_ref[s]) {
+            V.slot_ref[s] = 0;  // second chance
+          } else {
+            const unsigned long long st = ld_relaxed<SYS>(V.state + q);
+            if (st == (((unsigned long long)s << ST_SLOT_SHIFT) | ST_VALID) &&
+                (!V.wb || ld_relaxed_u32<SYS>(V.wb + q) == 0)) {
+              cand = true;
+              expect = st;
             }
           }
-          ok = __shfl_sync(0xffffffffu, ok, c);
-          if (ok) {
-            const unsigned long long sl = __shfl_sync(0xffffffffu, (unsigned long long)s, c);
-            if (lane == o) slot = sl;
-            pending &= ~(1u << o);
+          unsigned cmask = __ballot_sync(0xffffffffu, cand);
+          while (cmask && grp) {
+            const int c = __ffs(cmask) - 1;
+            cmask &= cmask - 1;
+            const int o = __ffs(grp) - 1;
+            const unsigned long long newp = __shfl_sync(0xffffffffu, (unsigned long long)lp, o);
+            int ok = 0;
+            if (lane == c) {
+              if (q == SLOT_EMPTY) {
+                ok = atom_cas_acq_rel<SYS>(V.slot_page + s, SLOT_EMPTY, newp) == SLOT_EMPTY;
+              } else if (atom_cas_acq_rel<SYS>(V.state + q, expect, 0ull) == expect) {
+                atom_exch_relaxed<SYS>(V.slot_page + s, newp);
+                atomicAdd(acc + K_EVICT, 1ull);
+                ok = 1;
+              }
+            }
+            ok = __shfl_sync(0xffffffffu, ok, c);
+            if (ok) {
+              const unsigned long long sl = __shfl_sync(0xffffffffu, (unsigned long long)s, c);
+              if (lane == o) slot = sl;
+              grp &= ~(1u << o);
+              pending &= ~(1u << o);
+            }
           }
         }
       }
       // owners without a slot give the fill up and read the backing store
       if ((pending >> lane) & 1u) {
-        atom_and_relaxed(stw, ~ST_BUSY);
+        atom_and_relaxed<SYS>(stw, ~ST_BUSY);
         cls = CLS_BYPASS;
       }
       unsigned fills = __ballot_sync(0xffffffffu, cls == CLS_OWN);
@@ -337,22 +423,24 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         fills &= fills - 1;
         const unsigned long long po = __shfl_sync(0xffffffffu, (unsigned long long)p, o);
         const unsigned long long so = __shfl_sync(0xffffffffu, (unsigned long long)slot, o);
-        copy_page(backing_addr(a.b, po, shift), a.c.slots + (so << shift), a.c.page_size, lane);
+        const uint32_t ow = __shfl_sync(0xffffffffu, owner, o);
+        copy_page(backing_addr(a.b, po, shift), a.c.sh[ow].slots + (so << shift), a.c.page_size, lane);
         __syncwarp();
         if (lane == o) {
-          __threadfence();
-          red_add_release(stw, (so << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
+          // the release reduction orders the warp's slot stores (made visible
+          // to this lane by __syncwarp) before the VALID bit
+          red_add_release<SYS>(stw, (so << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
           acc[K_READIO]++;  // only lane o touches it here
         }
       }
     }
 
-    // ---- 4. bounded wait for pages filled by other warps
+    // ---- 4. bounded wait for pages filled by other warps (or other GPUs)
     if (__any_sync(0xffffffffu, cls == CLS_WAIT)) {
       unsigned ns = 32;
       for (uint32_t it = 0;; it++) {
         if (cls == CLS_WAIT) {
-          const unsigned long long v = ld_acquire(stw);
+          const unsigned long long v = ld_acquire<SYS>(stw);
           if (v & ST_VALID) {
             cls = CLS_WAITED;
             slot = v >> ST_SLOT_SHIFT;
@@ -389,7 +477,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       if (gcls == CLS_BYPASS)
         src = backing_addr(a.b, p, shift) + in_page;
       else
-        src = a.c.slots + (gslot << shift) + in_page;
+        src = S.slots + (gslot << shift) + in_page;
       dst = orow + s0;
       len = s1 - s0;
     }
@@ -402,14 +490,15 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 
     // ---- release, clock reference bit, window-buffer consumption
     if (took_ref) {
-      red_add_release(stw, (unsigned long long)(-(long long)cnt));
-      if (gcls != CLS_BYPASS) a.c.slot_ref[gslot] = 1;
-      if (a.c.wb) wb_consume(a.c.wb + p, cnt);
+      red_add_release<SYS>(stw, (unsigned long long)(-(long long)cnt));
+      if (gcls != CLS_BYPASS) S.slot_ref[gslot] = 1;
+      if (S.wb) wb_consume<SYS>(S.wb + lp, cnt);
     }
 
     // ---- counters
     if (bad && sidx == 0) *reinterpret_cast<volatile int*>(a.host_err) = 1;
     const unsigned r0 = sidx == 0;
+    const bool cached = seg_ok && (gcls == CLS_HIT || gcls == CLS_OWN || gcls == CLS_WAITED);
     const unsigned n_rows_c = __popc(__ballot_sync(0xffffffffu, row_ok && r0));
     const unsigned n_cpu = __popc(__ballot_sync(0xffffffffu, pinned && r0));
     const unsigned n_bad = __popc(__ballot_sync(0xffffffffu, bad && r0));
@@ -421,6 +510,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const unsigned lm = __reduce_add_sync(0xffffffffu, seg_ok && (gcls == CLS_OWN || gcls == CLS_WAITED) ? len : 0u);
     const unsigned lb = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_BYPASS ? len : 0u);
     const unsigned lc = __reduce_add_sync(0xffffffffu, pinned && r0 ? len : 0u);
+    const unsigned lpeer = SYS ? __reduce_add_sync(0xffffffffu, cached && owner != a.c.rank ? len : 0u) : 0u;
     if (lane == 0) {
       acc[K_ROWS] += n_rows_c;
       acc[K_CPU] += n_cpu;
@@ -433,6 +523,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       acc[K_BMISS] += lm;
       acc[K_BBYP] += lb;
       acc[K_BCPU] += lc;
+      acc[K_BPEER] += lpeer;
     }
     __syncwarp();
   }
@@ -446,7 +537,8 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 }
 
 // Window buffering: one thread per node id, +1 on the pin counter of every
-// page its row touches (gids_kernel.cu:246-256 marks one page per id).
+// page its row touches, in the shard that owns the page (gids_kernel.cu:246-256
+// marks one page per id).
 __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.n) return;
@@ -455,33 +547,49 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   if (id < 0 || rs < 0 || (uint64_t)rs >= a.n_rows) return;  // the gather reports bad ids
   const uint64_t b0 = (uint64_t)rs * a.stride;
   const uint64_t p0 = b0 >> a.page_shift, p1 = (b0 + a.row_bytes - 1) >> a.page_shift;
-  for (uint64_t p = p0; p <= p1; p++) atomicAdd(a.wb + p, 1u);
+  for (uint64_t p = p0; p <= p1; p++) {
+    if (a.world == 1)
+      atomicAdd(a.wb[0] + p, 1u);
+    else
+      atomicAdd_system(a.wb[p % a.world] + p / a.world, 1u);
+  }
 }
 
 }  // namespace
 
-void launch_gather(const GatherArgs& a, int vec, int grid, cudaStream_t st) {
+template <bool SYS>
+static void launch_scoped(const GatherArgs& a, int vec, int grid, cudaStream_t st) {
   switch (vec) {
-    case 16: gather_kernel<16><<<grid, GATHER_THREADS, 0, st>>>(a); break;
-    case 8: gather_kernel<8><<<grid, GATHER_THREADS, 0, st>>>(a); break;
-    case 4: gather_kernel<4><<<grid, GATHER_THREADS, 0, st>>>(a); break;
-    case 2: gather_kernel<2><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 16: gather_kernel<16, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 8: gather_kernel<8, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 4: gather_kernel<4, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 2: gather_kernel<2, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
     default: throw Error(GIDS_E_INVAL, "unsupported vector width");
   }
+}
+
+void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st) {
+  if (sys)
+    launch_scoped<true>(a, vec, grid, st);
+  else
+    launch_scoped<false>(a, vec, grid, st);
   GIDS_CUDA(cudaGetLastError());
 }
 
-int gather_blocks_per_sm(int vec) {
+template <bool SYS>
+static int occupancy(int vec) {
   int n = 0;
   switch (vec) {
-    case 16: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<16>, GATHER_THREADS, 0)); break;
-    case 8: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<8>, GATHER_THREADS, 0)); break;
-    case 4: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<4>, GATHER_THREADS, 0)); break;
-    case 2: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<2>, GATHER_THREADS, 0)); break;
+    case 16: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<16, SYS>, GATHER_THREADS, 0)); break;
+    case 8: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<8, SYS>, GATHER_THREADS, 0)); break;
+    case 4: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<4, SYS>, GATHER_THREADS, 0)); break;
+    case 2: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<2, SYS>, GATHER_THREADS, 0)); break;
     default: throw Error(GIDS_E_INVAL, "unsupported vector width");
   }
   return n;
 }
+
+int gather_blocks_per_sm(int vec, bool sys) { return sys ? occupancy<true>(vec) : occupancy<false>(vec); }
 
 void launch_wb_mark(const WbArgs& a, cudaStream_t st) {
   if (!a.n) return;

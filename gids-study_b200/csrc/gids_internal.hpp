@@ -14,6 +14,10 @@
 
 #include "gids_b200.h"
 
+#ifndef GIDS_MAX_WORLD
+#define GIDS_MAX_WORLD 8
+#endif
+
 namespace gids {
 
 // ------------------------------------------------------------------ errors
@@ -65,17 +69,27 @@ constexpr uint64_t SLOT_EMPTY = ~0ull;
 enum : int { CLS_NONE = 0, CLS_HIT = 1, CLS_OWN = 2, CLS_WAIT = 3, CLS_WAITED = 4, CLS_BYPASS = 5 };
 
 // ---------------------------------------------------- device-side views
-struct DevCache {
-  unsigned long long* state;      // [n_pages] page table
-  unsigned long long* slot_page;  // [n_slots] page held by each slot (SLOT_EMPTY if none)
+// One shard of the page cache: the page table of the pages a rank owns
+// (page p is owned by rank p % world, at local index p / world) and that
+// rank's slots. Pointers are valid in the calling process: local memory, or
+// a peer's memory mapped through CUDA IPC or peer access.
+struct DevShard {
+  unsigned long long* state;      // [n_pages_local] page table
+  unsigned long long* slot_page;  // [n_slots] local page index held by each slot (SLOT_EMPTY if none)
   unsigned char* slot_ref;        // [n_slots] clock reference bit
-  unsigned int* wb;               // [n_pages] window-buffer pins, or nullptr
+  unsigned int* wb;               // [n_pages_local] window-buffer pins, or nullptr
   char* slots;                    // [n_slots * page_size] resident pages
   unsigned long long* clock;      // clock hand
-  uint64_t n_slots;
-  uint64_t n_pages;
+};
+
+struct DevCache {
+  DevShard sh[GIDS_MAX_WORLD];
+  uint64_t n_slots;  // slots per shard
+  uint64_t n_pages;  // pages of the whole range
   uint32_t page_shift;
   uint32_t page_size;
+  uint32_t world;  // ranks sharing the cache (1 = unsharded)
+  uint32_t rank;
 };
 
 struct DevBacking {
@@ -122,7 +136,8 @@ struct GatherArgs {
 };
 
 struct WbArgs {
-  unsigned int* wb;
+  unsigned int* wb[GIDS_MAX_WORLD];  // pin counters of every shard
+  uint32_t world;
   const int64_t* idx;
   uint64_t n;
   int64_t off;
@@ -132,11 +147,11 @@ struct WbArgs {
   uint32_t page_shift;
 };
 
-// Launchers (gather.cu).
-void launch_gather(const GatherArgs& a, int vec, int grid, cudaStream_t st);
+// Launchers (gather.cu). sys = the cache is shared with other GPUs, so
+// state-word atomics and fences use system scope.
+void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st);
 void launch_wb_mark(const WbArgs& a, cudaStream_t st);
-void launch_invalidate_all(const DevCache& c, cudaStream_t st);
-int gather_blocks_per_sm(int vec);
+int gather_blocks_per_sm(int vec, bool sys);
 constexpr int GATHER_THREADS = 256;
 
 // ------------------------------------------------------- emulated SSDs
@@ -225,7 +240,20 @@ class Store {
   uint64_t read_off_pages = 0, num_ele = 0, range_bytes = 0, n_pages = 0, n_slots = 0;
   uint32_t row_layout = 0;  // source row stride (elements) for CPU-buffer fills / WB; 0 = unknown
 
-  // device allocations
+  // sharding (page p is owned by rank p % world)
+  uint32_t world = 1, rank = 0;
+  uint64_t n_pages_local = 0;
+  bool shards_ready = true;           // false until peers are attached (world > 1)
+  DevShard shards[GIDS_MAX_WORLD] = {};
+  std::vector<void*> ipc_opened;      // peer shard bases opened through CUDA IPC
+  void set_sharding(uint32_t world, uint32_t rank);
+  void ipc_handle(void* out64);
+  void open_peers(const void* handles, uint32_t n);
+  static void share_in_process(Store* const* stores, uint32_t n);
+
+  // device allocations (this rank's shard lives in one allocation, d_shard)
+  char* d_shard = nullptr;
+  uint64_t shard_bytes = 0;
   unsigned long long* d_state = nullptr;
   unsigned long long* d_slot_page = nullptr;
   unsigned char* d_slot_ref = nullptr;
@@ -259,7 +287,7 @@ class Store {
   uint64_t total_access = 0;
   uint64_t launches = 0;
   void fold_events(bool wait);
-  int grid_blocks[5] = {0, 0, 0, 0, 0};
+  int grid_blocks[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
   std::mutex mu;
 
  private:

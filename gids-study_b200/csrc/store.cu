@@ -74,14 +74,110 @@ void Store::free_all() {
     if (p) cudaFree((void*)p);
     p = nullptr;
   };
-  f(d_state);
-  f(d_slot_page);
-  f(d_slot_ref);
-  f(d_wb);
-  f(d_slots);
+  for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
+  ipc_opened.clear();
+  if (world == 1) f(d_wb);  // sharded stores keep the pins inside the shard allocation
+  if (d_shard) cudaFree(d_shard);
+  d_shard = nullptr;
+  d_state = nullptr;
+  d_slot_page = nullptr;
+  d_slot_ref = nullptr;
+  d_wb = nullptr;
+  d_slots = nullptr;
   f(d_cpu_bits);
   f(d_cpu_rank);
   cpu_buf.release();
+}
+
+namespace {
+// Byte layout of one shard allocation; identical on every rank so that a
+// peer's shard can be addressed from its base pointer alone.
+struct ShardLayout {
+  uint64_t state, slot_page, slot_ref, wb, clock, slots, total;
+  ShardLayout(uint64_t n_pages_local, uint64_t n_slots, uint32_t page_size, bool with_wb) {
+    auto up = [](uint64_t v, uint64_t a) { return (v + a - 1) / a * a; };
+    state = 0;
+    slot_page = up(state + n_pages_local * 8, 256);
+    slot_ref = up(slot_page + n_slots * 8, 256);
+    wb = up(slot_ref + n_slots, 256);
+    clock = up(wb + (with_wb ? n_pages_local * 4 : 0), 256);
+    slots = up(clock + 8, page_size > 4096 ? page_size : 4096);
+    total = slots + n_slots * (uint64_t)page_size;
+  }
+  DevShard at(char* base, bool with_wb) const {
+    DevShard d{};
+    d.state = (unsigned long long*)(base + state);
+    d.slot_page = (unsigned long long*)(base + slot_page);
+    d.slot_ref = (unsigned char*)(base + slot_ref);
+    d.wb = with_wb ? (unsigned int*)(base + wb) : nullptr;
+    d.clock = (unsigned long long*)(base + clock);
+    d.slots = base + slots;
+    return d;
+  }
+};
+}  // namespace
+
+void Store::set_sharding(uint32_t w, uint32_t r) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(!initialized, GIDS_E_STATE, "set_sharding after init_controllers");
+  GIDS_CHECK(w >= 1 && w <= GIDS_MAX_WORLD && r < w, GIDS_E_INVAL, "need 1 <= world <= 8 and rank < world");
+  world = w;
+  rank = r;
+}
+
+void Store::ipc_handle(void* out64) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized && d_shard, GIDS_E_STATE, "no shard allocated yet");
+  DeviceGuard g(device);
+  cudaIpcMemHandle_t h;
+  GIDS_CUDA(cudaIpcGetMemHandle(&h, d_shard));
+  memcpy(out64, &h, sizeof(h));
+}
+
+void Store::open_peers(const void* handles, uint32_t n) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "open_peers before init_controllers");
+  GIDS_CHECK(n == world, GIDS_E_INVAL, "need one handle per rank");
+  DeviceGuard g(device);
+  const ShardLayout L(n_pages_local, n_slots, page_size, world > 1);
+  const cudaIpcMemHandle_t* h = (const cudaIpcMemHandle_t*)handles;
+  for (uint32_t r = 0; r < world; r++) {
+    if (r == rank) continue;
+    void* p = nullptr;
+    GIDS_CUDA(cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess));
+    ipc_opened.push_back(p);
+    shards[r] = L.at((char*)p, world > 1);
+  }
+  shards_ready = true;
+}
+
+void Store::share_in_process(Store* const* stores, uint32_t n) {
+  GIDS_CHECK(n >= 1 && n <= GIDS_MAX_WORLD, GIDS_E_INVAL, "1..8 stores");
+  for (uint32_t i = 0; i < n; i++) {
+    Store* s = stores[i];
+    GIDS_CHECK(s && s->initialized, GIDS_E_STATE, "every store must be initialised");
+    GIDS_CHECK(s->world == n && s->rank == i, GIDS_E_INVAL, "store i must have world n and rank i");
+    GIDS_CHECK(s->n_pages == stores[0]->n_pages && s->n_slots == stores[0]->n_slots &&
+                   s->page_size == stores[0]->page_size,
+               GIDS_E_INVAL, "stores differ in geometry");
+  }
+  for (uint32_t i = 0; i < n; i++)
+    for (uint32_t j = 0; j < n; j++) {
+      const int di = stores[i]->device, dj = stores[j]->device;
+      if (di == dj) continue;
+      DeviceGuard g(di);
+      cudaError_t e = cudaDeviceEnablePeerAccess(dj, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+      } else {
+        GIDS_CUDA(e);
+      }
+    }
+  for (uint32_t i = 0; i < n; i++) {
+    std::lock_guard<std::mutex> lk(stores[i]->mu);
+    for (uint32_t j = 0; j < n; j++) stores[i]->shards[j] = stores[j]->shards[j];
+    stores[i]->shards_ready = true;
+  }
 }
 
 void Store::init_controllers(Controllers* c, uint32_t ps, uint64_t read_off_pages_, uint64_t cache_mb, uint64_t ne,
@@ -107,35 +203,43 @@ void Store::init_controllers(Controllers* c, uint32_t ps, uint64_t read_off_page
   c->register_with_cuda();
   ctrls = c;
 
-  GIDS_CUDA(cudaMalloc(&d_state, n_pages * sizeof(unsigned long long)));
-  GIDS_CUDA(cudaMemset(d_state, 0, n_pages * sizeof(unsigned long long)));
-  if (n_slots) {
-    GIDS_CUDA(cudaMalloc(&d_slot_page, n_slots * sizeof(unsigned long long)));
-    GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
-    GIDS_CUDA(cudaMalloc(&d_slot_ref, n_slots));
-    GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
-    GIDS_CUDA(cudaMalloc(&d_slots, n_slots * (uint64_t)ps));
-  }
+  // this rank's shard: page table of the pages it owns (p % world == rank),
+  // slots, clock and (when sharded) window-buffer pins, in one allocation
+  n_pages_local = (n_pages + world - 1) / world;
+  const bool with_wb = world > 1;
+  const ShardLayout L(n_pages_local, n_slots, ps, with_wb);
+  shard_bytes = L.total;
+  GIDS_CUDA(cudaMalloc(&d_shard, shard_bytes));
+  const DevShard mine = L.at(d_shard, with_wb);
+  d_state = mine.state;
+  d_slot_page = mine.slot_page;
+  d_slot_ref = mine.slot_ref;
+  d_slots = mine.slots;
+  if (with_wb) d_wb = mine.wb;
+  GIDS_CUDA(cudaMemset(d_shard, 0, L.slot_page));
+  GIDS_CUDA(cudaMemset(d_shard + L.slot_page, 0xFF, n_slots * 8));
+  GIDS_CUDA(cudaMemset(d_shard + L.slot_ref, 0, L.slots - L.slot_ref));
+  shards[rank] = mine;
+  shards_ready = world == 1;
   int sms = 0;
   GIDS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   const int vecs[4] = {16, 8, 4, 2};
-  for (int i = 0; i < 4; i++) grid_blocks[i] = std::max(1, gather_blocks_per_sm(vecs[i])) * sms;
+  for (int sy = 0; sy < 2; sy++)
+    for (int i = 0; i < 4; i++) grid_blocks[sy][i] = std::max(1, gather_blocks_per_sm(vecs[i], sy == 1)) * sms;
   GIDS_CUDA(cudaDeviceSynchronize());
   initialized = true;
 }
 
 DevCache Store::dev_cache() const {
   DevCache c{};
-  c.state = d_state;
-  c.slot_page = d_slot_page;
-  c.slot_ref = d_slot_ref;
-  c.wb = d_wb;
-  c.slots = d_slots;
-  c.clock = d_clock;
+  for (uint32_t r = 0; r < world; r++) c.sh[r] = shards[r];
+  if (world == 1) c.sh[0].wb = d_wb;  // allocated on first use
   c.n_slots = n_slots;
   c.n_pages = n_pages;
   c.page_shift = page_shift;
   c.page_size = page_size;
+  c.world = world;
+  c.rank = rank;
   return c;
 }
 
@@ -196,6 +300,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
                        int cache_dim, const uint64_t* key_offs, cudaStream_t st) {
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(initialized, GIDS_E_STATE, "read_feature before init_controllers");
+  GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   GIDS_CHECK(k >= 0, GIDS_E_INVAL, "k must be >= 0");
   GIDS_CHECK(dim > 0 && cache_dim > 0 && dim <= cache_dim, GIDS_E_INVAL, "need 0 < dim <= cache_dim");
   DeviceGuard g(device);
@@ -270,7 +375,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
     a.total_chunks = chunks;
     const int vi = vec == 16 ? 0 : vec == 8 ? 1 : vec == 4 ? 2 : 3;
     const uint64_t want_blocks = (chunks + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
-    const int grid = (int)std::min<uint64_t>(want_blocks, (uint64_t)grid_blocks[vi]);
+    const int grid = (int)std::min<uint64_t>(want_blocks, (uint64_t)grid_blocks[world > 1 ? 1 : 0][vi]);
     EvPair ev;
     if (!ev_free.empty()) {
       ev = ev_free.back();
@@ -280,7 +385,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
       GIDS_CUDA(cudaEventCreate(&ev.b));
     }
     GIDS_CUDA(cudaEventRecord(ev.a, st));
-    launch_gather(a, vec, grid, st);
+    launch_gather(a, vec, world > 1, grid, st);
     launches++;
     GIDS_CUDA(cudaEventRecord(ev.b, st));
     ev_pending.push_back(ev);
@@ -301,6 +406,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   GIDS_CHECK(n >= 0, GIDS_E_INVAL, "n must be >= 0");
   if (n == 0) return;
   GIDS_CHECK(idx, GIDS_E_INVAL, "null index pointer");
+  GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   DeviceGuard g(device);
   if (!d_wb) {
     GIDS_CUDA(cudaMalloc(&d_wb, n_pages * sizeof(unsigned int)));
@@ -310,7 +416,8 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   // (the reference's assumption, gids_kernel.cu:251-252)
   uint32_t se = stride_elems ? stride_elems : row_layout ? row_layout : page_size / elem_bytes;
   WbArgs w{};
-  w.wb = d_wb;
+  w.world = world;
+  for (uint32_t r = 0; r < world; r++) w.wb[r] = world == 1 ? d_wb : shards[r].wb;
   w.idx = idx;
   w.n = (uint64_t)n;
   w.off = off;
@@ -441,7 +548,8 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
     backing_write(*ctrls, src, nbytes, off);
   }
   // the cache and the CPU buffer may hold stale copies of the written pages
-  GIDS_CUDA(cudaMemset(d_state, 0, n_pages * sizeof(unsigned long long)));
+  // (a sharded cache drops this rank's shard; every rank has to flush)
+  GIDS_CUDA(cudaMemset(d_state, 0, n_pages_local * sizeof(unsigned long long)));
   if (n_slots) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
@@ -452,12 +560,13 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
 
 void Store::flush_cache() {
   // The cache never holds dirty pages (writes go straight to the backing
-  // store), so flushing only has to drop every resident page.
+  // store), so flushing only has to drop every resident page. A sharded
+  // cache drops this rank's shard: all ranks flush, with no gather in flight.
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(initialized, GIDS_E_STATE, "flush_cache before init_controllers");
   DeviceGuard g(device);
   GIDS_CUDA(cudaDeviceSynchronize());
-  GIDS_CUDA(cudaMemset(d_state, 0, n_pages * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_state, 0, n_pages_local * sizeof(unsigned long long)));
   if (n_slots) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));

@@ -79,6 +79,21 @@ GIDS_API int gids_ctrls_init(gids_ctrls_t *c, uint32_t n_ctrls, uint64_t q_depth
  * where page p mod (n_ctrls * data_pages_per_ssd) is). */
 GIDS_API int gids_ctrls_set_emulation(gids_ctrls_t *c, uint64_t capacity_bytes_per_ssd, const char *path_pattern);
 GIDS_API int gids_ctrls_destroy(gids_ctrls_t *c);
+/* Backing-store access without a GPU cache (no reference counterpart; the
+ * reference writes its SSDs with tensor_write.py / nvm-readwrite_stripe-bench):
+ * bind sizes and maps the first num_ssd SSDs for a range of range_bytes with
+ * the given page size and first page read_off_pages (what
+ * gids_store_init_controllers does; a later store with the same geometry
+ * reuses the binding); write/read move host bytes through the stripe map;
+ * fill_synthetic writes the synthetic stream of gids_fill_synthetic. No GPU
+ * is needed until a store uses the controllers. */
+GIDS_API int gids_ctrls_bind(gids_ctrls_t *c, uint32_t num_ssd, uint32_t page_size, uint64_t read_off_pages,
+                             uint64_t range_bytes);
+GIDS_API int gids_ctrls_write(gids_ctrls_t *c, const void *src, uint64_t nbytes, uint64_t offset_bytes);
+GIDS_API int gids_ctrls_read(gids_ctrls_t *c, void *dst, uint64_t nbytes, uint64_t offset_bytes);
+GIDS_API int gids_ctrls_fill_synthetic(gids_ctrls_t *c, int kind, uint64_t seed, int threads);
+/* [0]=pages in the range, [1]=pages physically held, [2]=bytes per SSD, [3]=SSDs bound */
+GIDS_API int gids_ctrls_geometry(gids_ctrls_t *c, uint64_t *out, int count);
 
 /* --------------------------------------------------------------- store --
  * Replaces BAM_Feature_Store<T>'s default constructor (gids_nvme.cu:812-815,
@@ -100,6 +115,25 @@ GIDS_API int gids_store_set_synchronous(gids_store_t *s, int synchronous);
  * the first gather tells it (the reference assumes one row per page,
  * gids_nvme.cu:173,704). */
 GIDS_API int gids_store_set_row_layout(gids_store_t *s, uint32_t cache_dim);
+
+/* ------------------------------------------------------ sharded cache --
+ * No reference counterpart (the reference caches on one GPU). W stores, one
+ * per GPU, share one page cache: page p is owned by rank p % W, whose HBM
+ * holds its page-table entry and, when resident, its data; every GPU looks
+ * pages up in the owner's shard and reads hits over NVLink, and a miss fills
+ * the owner's slot. Call gids_store_set_sharding before
+ * gids_store_init_controllers (all ranks with the same geometry), then either
+ *   - one process per GPU: exchange the 64-byte gids_store_ipc_handle of
+ *     every rank (e.g. an all-gather) and call gids_store_open_peers on
+ *     each rank with the handles in rank order; or
+ *   - one process for all GPUs: gids_store_share_shards(stores, W).
+ * Gathers fail with GIDS_E_STATE until the peers are attached. A rank's
+ * shard must outlive every gather of every rank (destroy after a barrier);
+ * flush_cache and writes drop only the calling rank's shard. */
+GIDS_API int gids_store_set_sharding(gids_store_t *s, int world, int rank);
+GIDS_API int gids_store_ipc_handle(gids_store_t *s, void *out, size_t len);
+GIDS_API int gids_store_open_peers(gids_store_t *s, const void *handles, int world);
+GIDS_API int gids_store_share_shards(gids_store_t *const *stores, int n);
 
 /* -------------------------------------------------------------- gathers --
  * gids_read_feature replaces BAM_Feature_Store<T>::read_feature
@@ -161,7 +195,8 @@ GIDS_API int gids_flush_cpu_access_count(gids_store_t *s);
 #define GIDS_STAT_BYTES_CPU 12
 #define GIDS_STAT_EVICTIONS 13
 #define GIDS_STAT_LAUNCHES 14    /* gather kernels launched */
-#define GIDS_STAT_COUNT 16
+#define GIDS_STAT_BYTES_PEER 15  /* output bytes copied from another GPU's shard (NVLink) */
+#define GIDS_STAT_COUNT 20
 /* Copies the cumulative counters (synchronizes the store's last stream). */
 GIDS_API int gids_get_stats(gids_store_t *s, uint64_t *out, int count);
 GIDS_API int gids_reset_stats(gids_store_t *s);

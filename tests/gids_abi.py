@@ -15,7 +15,8 @@ GIDS_E_STATE = -4
 GIDS_E_RANGE = -5
 GIDS_E_UNSUPPORTED = -7
 STAT_NAMES = ["access", "hit", "miss", "read_io", "bypass", "cpu_rows", "rows", "wait_timeouts", "bad_ids",
-              "bytes_hit", "bytes_miss", "bytes_bypass", "bytes_cpu", "evictions", "launches"]
+              "bytes_hit", "bytes_miss", "bytes_bypass", "bytes_cpu", "evictions", "launches", "bytes_peer"]
+N_STATS = 20
 
 _lib = None
 
@@ -35,6 +36,11 @@ def lib():
             "gids_ctrls_init": (i32, [vp, u32, u64, u64, P(ctypes.c_int32)]),
             "gids_ctrls_set_emulation": (i32, [vp, u64, ctypes.c_char_p]),
             "gids_ctrls_destroy": (i32, [vp]),
+            "gids_ctrls_bind": (i32, [vp, u32, u32, u64, u64]),
+            "gids_ctrls_write": (i32, [vp, vp, u64, u64]),
+            "gids_ctrls_read": (i32, [vp, vp, u64, u64]),
+            "gids_ctrls_fill_synthetic": (i32, [vp, i32, u64, i32]),
+            "gids_ctrls_geometry": (i32, [vp, P(u64), i32]),
             "gids_store_create": (i32, [P(vp), u32, i32]),
             "gids_store_init_controllers": (i32, [vp, vp, u32, u64, u64, u64, u64]),
             "gids_store_destroy": (i32, [vp]),
@@ -59,6 +65,10 @@ def lib():
             "gids_read_range_host": (i32, [vp, vp, u64, u64]),
             "gids_fill_synthetic": (i32, [vp, i32, u64, i32]),
             "gids_store_geometry": (i32, [vp, P(u64), i32]),
+            "gids_store_set_sharding": (i32, [vp, i32, i32]),
+            "gids_store_ipc_handle": (i32, [vp, vp, ctypes.c_size_t]),
+            "gids_store_open_peers": (i32, [vp, vp, i32]),
+            "gids_store_share_shards": (i32, [P(vp), i32]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -92,7 +102,7 @@ class Store:
     """Thin owner of a gids_store_t + gids_ctrls_t pair."""
 
     def __init__(self, elem_bytes, page_size, num_ele, cache_mb, num_ssd=1, ssd_list=None, read_off_pages=0,
-                 capacity=0, pattern=None, device=0, synchronous=True):
+                 capacity=0, pattern=None, device=0, synchronous=True, world=1, rank=0):
         L = lib()
         self.c = ctypes.c_void_p()
         check(L.gids_ctrls_create(ctypes.byref(self.c)))
@@ -102,6 +112,8 @@ class Store:
             check(L.gids_ctrls_set_emulation(self.c, capacity, (pattern or "").encode()))
         self.s = ctypes.c_void_p()
         check(L.gids_store_create(ctypes.byref(self.s), elem_bytes, device))
+        if world > 1:
+            check(L.gids_store_set_sharding(self.s, world, rank))
         check(L.gids_store_init_controllers(self.s, self.c, page_size, read_off_pages, cache_mb, num_ele, num_ssd))
         check(L.gids_store_set_synchronous(self.s, 1 if synchronous else 0))
         self.elem_bytes = elem_bytes
@@ -136,9 +148,9 @@ class Store:
         return lib().gids_read_feature_multi(self.s, k, O, I, N, dim, cache_dim, K, stream)
 
     def stats(self):
-        v = (ctypes.c_uint64 * 16)()
-        check(lib().gids_get_stats(self.s, v, 16))
-        return dict(zip(STAT_NAMES, list(v)[:15]))
+        v = (ctypes.c_uint64 * N_STATS)()
+        check(lib().gids_get_stats(self.s, v, N_STATS))
+        return dict(zip(STAT_NAMES, list(v)[:len(STAT_NAMES)]))
 
     def reset_stats(self):
         check(lib().gids_reset_stats(self.s))
