@@ -51,15 +51,18 @@ for _p in (REPO, PKG):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+BASE = dict(cpu_pin_frac=0.0, wb=0, phys_gb=64.0)
 CONFIGS = {
-    # name: nodes, mean degree, zipf alpha, dim, dtype, page, ssds, cache MB, fanouts, batch, seed zipf
-    "c1": dict(nodes=1_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=1,
+    # nodes, mean degree, zipf alpha of the out-degree, feature dim/dtype, page size, emulated SSDs,
+    # cache MB per GPU, fanouts, seed batch, seed law (None = uniform), pinned fraction, WB depth
+    "c1": dict(BASE, nodes=1_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=1,
                cache_mb=4096, fanouts=[10, 5], batch=1024, seed_zipf=None),
-    "c2": dict(nodes=100_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=4,
+    "c2": dict(BASE, nodes=100_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=4,
                cache_mb=40 * 1024, fanouts=[15, 10, 5], batch=4096, seed_zipf=None),
-    "c4": dict(nodes=50_000_000, mean_deg=15, alpha=1.2, dim=768, dtype="float16", page=4096, ssds=4,
-               cache_mb=8 * 1024, fanouts=[10, 10], batch=2048, seed_zipf=1.0),
-    "c5": dict(nodes=500_000_000, mean_deg=10, alpha=1.1, dim=128, dtype="float32", page=4096, ssds=8,
+    "c4": dict(BASE, nodes=50_000_000, mean_deg=15, alpha=1.2, dim=768, dtype="float16", page=4096, ssds=4,
+               cache_mb=8 * 1024, fanouts=[10, 10], batch=2048, seed_zipf=1.0, cpu_pin_frac=0.01, wb=8,
+               phys_gb=80.0),
+    "c5": dict(BASE, nodes=500_000_000, mean_deg=10, alpha=1.1, dim=128, dtype="float32", page=4096, ssds=8,
                cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None),
 }
 KIND = {"float32": 1, "float16": 2}
@@ -178,12 +181,16 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
-def make_batches(cfg, n_batches, rank, device):
-    """Input-node ids of n_batches minibatches from the seeded graph and sampler."""
-    from GIDS.synthetic import NeighborSampler, SyntheticGraph, seed_batches
+def make_batches(cfg, n_batches, rank, device, with_pins=False):
+    """Input-node ids of n_batches minibatches from the seeded graph and
+    sampler, and (with_pins) the PageRank pin list of the constant CPU buffer."""
+    from GIDS.synthetic import NeighborSampler, SyntheticGraph, pagerank_pin_list, seed_batches
 
     t0 = time.time()
     g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
+    pins = None
+    if with_pins and cfg["cpu_pin_frac"] > 0:
+        pins = pagerank_pin_list(g, cfg["cpu_pin_frac"])
     s = NeighborSampler(g, cfg["fanouts"], seed=sampler_seed(rank))
     seeds = seed_batches(cfg["nodes"], cfg["batch"], n_batches, sampler_seed(rank), device=device,
                          zipf_alpha=cfg["seed_zipf"])
@@ -194,6 +201,8 @@ def make_batches(cfg, n_batches, rank, device):
     del g, s
     if device != "cpu":
         torch.cuda.synchronize()
+    if with_pins:
+        return out, pins, time.time() - t0
     return out, time.time() - t0
 
 
@@ -275,7 +284,7 @@ def run_ours(args, cfg, dist: Dist):
     row_bytes = dim * esize
     num_ele = cfg["nodes"] * dim
     range_bytes = num_ele * esize
-    phys = min(int(args.phys_gb * 1e9), range_bytes)
+    phys = min(int(cfg["phys_gb"] * 1e9), range_bytes)
     per_ssd = (phys // cfg["ssds"]) // page * page
     shared = dist.world > 1
     pattern = f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd{{}}" if shared else None
@@ -299,7 +308,8 @@ def run_ours(args, cfg, dist: Dist):
     g = GIDS.GIDS(page_size=page, off=0, cache_dim=dim, num_ele=num_ele, num_ssd=cfg["ssds"],
                   ssd_list=list(range(cfg["ssds"])), cache_size=cfg["cache_mb"], ctrl_idx=dist.local,
                   dtype=TDTYPE[dt], ssd_capacity=per_ssd if phys < range_bytes else 0, ssd_path=pattern,
-                  synchronous=False, shard_cache=shared and not args.no_shard)
+                  synchronous=False, shard_cache=shared and not args.no_shard, window_buffer=cfg["wb"] > 0,
+                  wb_size=max(1, cfg["wb"]))
     t_store = time.time() - t0
     if not shared:
         t0 = time.time()
@@ -308,23 +318,26 @@ def run_ours(args, cfg, dist: Dist):
     geo = g.BAM_FS.geometry()
     log(f"[rank {dist.rank}] store ready: {geo} (alloc {t_store:.1f}s, fill {t_fill:.1f}s)")
 
-    n_batches = args.warmup + 2 * args.steps
-    batches, t_sample = make_batches(cfg, n_batches, dist.rank, device)
+    wb = cfg["wb"]
+    # each timed loop consumes `steps` batches; window buffering reads wb batches ahead
+    n_batches = args.warmup + 2 * (args.steps + wb)
+    batches, pins, t_sample = make_batches(cfg, n_batches, dist.rank, device, with_pins=True)
     sizes = [int(b.numel()) for b in batches]
     log(f"[rank {dist.rank}] sampled {n_batches} minibatches in {t_sample:.1f}s, input nodes mean "
         f"{np.mean(sizes):.0f}")
+    if pins is not None:
+        g.cpu_backing_buffer(dim, int(pins.numel()))
+        g.set_cpu_buffer(pins, int(pins.numel()))
+        log(f"[rank {dist.rank}] constant CPU buffer: {pins.numel()} pinned rows (PageRank top "
+            f"{cfg['cpu_pin_frac']:.0%})")
     host_batches = [b.cpu().pin_memory() for b in batches]
-    out = torch.empty((max(sizes), dim), dtype=TDTYPE[dt], device=device)
     stream = torch.cuda.current_stream(device)
-    sh = stream.cuda_stream
     bam = g.BAM_FS
-
-    def gather_dev(ids):
-        bam.read_feature(out.data_ptr(), ids.data_ptr(), ids.numel(), dim, dim, 0, sh)
+    dev_it = iter([[b] for b in batches[:args.warmup + args.steps + wb]])
 
     # warm-up (fills the cache)
     for i in range(args.warmup):
-        gather_dev(batches[i])
+        g.fetch_feature(dim, dev_it, device)
     torch.cuda.synchronize()
     bam.reset_stats()
 
@@ -340,8 +353,8 @@ def run_ours(args, cfg, dist: Dist):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("gids_timed_value")
     ev0.record(stream)
-    for ids in dev_ids:
-        gather_dev(ids)
+    for _ in dev_ids:
+        g.fetch_feature(dim, dev_it, device)
     ev1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -351,11 +364,18 @@ def run_ours(args, cfg, dist: Dist):
     st = bam.get_stats()
     k_ms = bam.kernel_time_ms()
     launches = st["launches"]
-    rows_val = sum(int(b.numel()) for b in dev_ids)
+    rows_val = st["rows"]
 
     # ---- timed region 2: end to end through GIDS.fetch_feature, ids in pinned host memory
-    e2e_batches = host_batches[args.warmup + args.steps:]
-    it = iter([[b] for b in e2e_batches])
+    g.window_buffer.clear()  # a fresh iterator starts a fresh window
+    g.wb_init = False
+    first = args.warmup + args.steps + wb
+    e2e_batches = host_batches[first:first + args.steps]
+    it = iter([[b] for b in host_batches[first:]])
+    if wb:  # the window of a fresh epoch is filled before the timed steps
+        g.fill_wb(it, wb)
+        g.wb_init = True
+    torch.cuda.synchronize()
     bam.reset_stats()
     dist.barrier()
     torch.cuda.synchronize()
@@ -374,7 +394,7 @@ def run_ours(args, cfg, dist: Dist):
     dist.barrier()
     t_e2e = e0.elapsed_time(e1) / 1e3
     st_e2e = bam.get_stats()
-    rows_e2e = sum(int(b.numel()) for b in e2e_batches)
+    rows_e2e = st_e2e["rows"]
 
     # ---- aggregate over ranks
     t_val_max = dist.max(t_val)
@@ -432,18 +452,19 @@ def run_ours(args, cfg, dist: Dist):
                                      "wrap_pages": geo["wrap_pages"]},
                    "l2": (f"no flush: every step reads {min(sizes) * row_bytes / 1e9:.2f} GB or more (L2 is 126 MB)"
                           if min(sizes) * row_bytes > 4 * 126e6 else "steps smaller than 4x L2: not a timing run"),
-                   "input_nodes_per_step": round(float(np.mean(sizes[args.warmup:args.warmup + args.steps])), 1)},
+                   "input_nodes_per_step": round(rows_val / max(1, len(dev_ids)), 1),
+                   "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
+                   "window_buffer_depth": wb},
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "api": "GIDS.fetch_feature",
                 "h2d_bytes_per_step": int(np.mean([b.numel() * 8 for b in e2e_batches])),
                 "d2h_bytes_per_step": esize, "wall_s": round(wall_e2e, 3),
                 "minibatches_per_s": round(dist.sum(len(e2e_batches)) / t_e2e_max, 3),
                 "mix": {"hit": round(st_e2e["hit"] / max(1, st_e2e["access"]), 4)}},
-        "gpu_launches": int(launches),
+        "gpu_launches": int(launches) + (len(dev_ids) if wb else 0),
         "clocks": clk,
         "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1)},
     }
-    del out
     torch.cuda.synchronize()
     return result, batches
 
@@ -482,7 +503,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--phys-gb", type=float, default=64.0, help="GB of pages the emulated SSDs hold")
+    ap.add_argument("--phys-gb", type=float, default=0.0, help="GB of pages the emulated SSDs hold (0: the config's)")
     ap.add_argument("--cpu-file-gb", type=float, default=8.0, help="size of the CPU-baseline memmap")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--nodes", type=int, default=0, help="override the node count (small profiling cases)")
@@ -501,6 +522,8 @@ def main():
         cfg["cache_mb"] = args.cache_mb
     if args.batch:
         cfg["batch"] = args.batch
+    if args.phys_gb:
+        cfg["phys_gb"] = args.phys_gb
 
     dist = Dist()
     if args.impl == "reference":

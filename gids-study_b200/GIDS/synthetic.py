@@ -188,23 +188,71 @@ class NeighborSampler:
 
 
 def seed_batches(num_nodes: int, batch_size: int, n_batches: int, seed: int, device="cpu", zipf_alpha=None):
-    """Seed-node batches: uniform over [0, N) or, with zipf_alpha, Zipf over node ids."""
+    """Batches of distinct seed nodes: uniform over [0, N) or, with zipf_alpha,
+    Zipf over node ids (ranks scattered over the id space by a hash)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(int(seed))
-    out = []
-    for _ in range(n_batches):
-        if zipf_alpha is None:
-            s = torch.randint(0, num_nodes, (batch_size * 2,), generator=gen, device=device)
+    a = None if zipf_alpha is None else float(zipf_alpha)
+
+    def draw(m):
+        if a is None:
+            return torch.randint(0, num_nodes, (m,), generator=gen, device=device)
+        u = torch.rand(m, generator=gen, device=device, dtype=torch.float64)
+        if abs(a - 1.0) < 1e-9:
+            r = torch.exp(u * math.log(num_nodes))
         else:
-            # inverse-CDF sampling of a Zipf law over ranks 1..N, ranks scattered over ids
-            u = torch.rand(batch_size * 2, generator=gen, device=device, dtype=torch.float64)
-            a = float(zipf_alpha)
-            if abs(a - 1.0) < 1e-9:
-                r = torch.exp(u * math.log(num_nodes))
-            else:
-                r = (1 + u * (num_nodes ** (1 - a) - 1)) ** (1 / (1 - a))
-            rank = r.to(torch.int64).clamp_(0, num_nodes - 1)
-            s = _srl(_mix(rank * int(_G) + 77), 1) % num_nodes
-        s = unique_first(s)[:batch_size]
-        out.append(s)
+            r = (1 + u * (num_nodes ** (1 - a) - 1)) ** (1 / (1 - a))
+        rank = r.to(torch.int64).clamp_(0, num_nodes - 1)
+        return _srl(_mix(rank * int(_G) + 77), 1) % num_nodes
+
+    out = []
+    batch_size = min(batch_size, num_nodes)
+    for _ in range(n_batches):
+        s = unique_first(draw(batch_size * 2))
+        for _ in range(64):  # skewed laws repeat ids: keep drawing until the batch is full
+            if s.numel() >= batch_size:
+                break
+            more = draw(batch_size * 4)
+            s = unique_first(torch.cat([s, more]))
+        out.append(s[:batch_size])
     return out
+
+
+def pagerank_pin_list(graph: SyntheticGraph, fraction: float = 0.01, damping: float = 0.85, iters: int = 20,
+                      chunk_rows: int = 1 << 22):
+    """pin_file for the constant CPU buffer: the top ``fraction`` of nodes by
+    the reference's in-degree-normalised ("reverse") PageRank.
+
+    Restates compute_pagerank (evaluation/page_rank_node_list_gen.py:126-134)
+    and the top-k of :282-285: pv = 1/N; K times: pv = pv / in_degree;
+    pv[v] = sum of pv[u] over the in-edges u -> v (copy_u + sum);
+    pv = (1 - d)/N + d * pv. The reference divides by a zero in-degree and
+    propagates inf/NaN from such nodes; here their share is 0 (guard).
+    Edges are generated and summed in chunks of ``chunk_rows`` destination
+    rows; returns the node ids, highest rank first (int64)."""
+    g = graph
+    dev = g.device
+    N = g.N
+    deg = g.in_degree(torch.arange(N, device=dev))
+    inv = torch.where(deg > 0, 1.0 / deg.clamp(min=1).to(torch.float64), torch.zeros((), dtype=torch.float64,
+                                                                                     device=dev))
+    # explicit CSC, built once per chunk of destination rows, kept as int32 sources
+    chunks = []
+    for lo in range(0, N, chunk_rows):
+        hi = min(N, lo + chunk_rows)
+        v = torch.arange(lo, hi, device=dev)
+        d = deg[lo:hi]
+        rows = torch.repeat_interleave(v, d)
+        start = torch.cumsum(d, 0) - d
+        j = torch.arange(rows.numel(), device=dev) - torch.repeat_interleave(start, d)
+        src = g.in_neighbor(rows, j)
+        chunks.append((lo, hi, (rows - lo).to(torch.int32), src.to(torch.int64 if N >= (1 << 31) else torch.int32)))
+    pv = torch.full((N,), 1.0 / N, dtype=torch.float64, device=dev)
+    for _ in range(iters):
+        norm = pv * inv
+        new = torch.zeros_like(pv)
+        for lo, hi, rows, src in chunks:
+            new[lo:hi].index_add_(0, rows.to(torch.int64), norm[src.to(torch.int64)])
+        pv = (1.0 - damping) / N + damping * new
+    k = max(1, int(N * fraction))
+    return torch.topk(pv, k, largest=True).indices

@@ -97,27 +97,39 @@ def test_gather_refused_before_peers_attached():
 def test_in_process_shards_one_gpu(world):
     rows, cdim = 12000, 1024
     t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 21, rows, cdim)
-    sh = Shared(t, world, cache_mb=8)  # 2048 slots per shard
+    sh = Shared(t, world, cache_mb=64)  # 16384 slots per shard: nothing is evicted
     rng = np.random.default_rng(world)
     try:
         ids = rng.integers(0, rows, size=5000)
         out = sh.gather(0, ids, cdim, cdim)
         assert bits_equal(out, oracle.gather(t, ids))
         st0 = sh.stats(0)
-        assert st0["bytes_peer"] > 0 and st0["read_io"] > 0
-        # the same ids from every other rank: its pages were filled into their owners' shards
+        assert st0["bytes_peer"] > 0 and st0["read_io"] > 0 and st0["evictions"] == 0
+        # the same ids from every other rank: the pages sit in their owners' shards
         for r in range(1, world):
             out = sh.gather(r, ids, cdim, cdim)
             assert bits_equal(out, oracle.gather(t, ids))
             st = sh.stats(r)
             assert st["miss"] == 0 and st["bypass"] == 0 and st["hit"] == st["access"]
             assert st["bytes_peer"] > 0
-        # churn: small shards evict, ranks alternate, results stay exact
-        for k in range(6):
+    finally:
+        sh.close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_in_process_shards_churn(world):
+    rows, cdim = 12000, 1024
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 23, rows, cdim)
+    sh = Shared(t, world, cache_mb=1)  # 256 slots per shard
+    rng = np.random.default_rng(10 + world)
+    try:
+        for k in range(8):
             ids = rng.integers(0, rows, size=7000)
             out = sh.gather(k % world, ids, cdim, cdim)
             assert bits_equal(out, oracle.gather(t, ids))
-        assert sum(sh.stats(r)["evictions"] for r in range(world)) > 0
+        tot = [sh.stats(r) for r in range(world)]
+        assert sum(s["evictions"] for s in tot) > 0
+        assert all(s["access"] == s["hit"] + s["miss"] + s["bypass"] for s in tot)
     finally:
         sh.close()
 

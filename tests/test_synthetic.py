@@ -1,0 +1,88 @@
+"""Synthetic graph, neighbour sampler and PageRank pin list (the inputs of the
+benchmarks), checked on CPU against an explicit CSC of the same graph."""
+import numpy as np
+import torch
+
+from GIDS.synthetic import (NeighborSampler, SyntheticGraph, pagerank_pin_list, seed_batches, unique_first,
+                            zipf_truncation)
+
+
+def test_zipf_truncation_reaches_mean():
+    for alpha, mean in [(1.1, 15), (1.2, 15), (1.0, 8), (1.1, 10)]:
+        K = zipf_truncation(alpha, mean)
+        k = np.arange(1, K + 1, dtype=np.float64)
+        w = k ** -alpha
+        assert (k * w).sum() / w.sum() >= mean
+        k = k[:-1]
+        w = w[:-1]
+        assert (k * w).sum() / w.sum() < mean
+
+
+def test_graph_degrees_and_determinism():
+    g = SyntheticGraph(50000, 15, 1.1, seed=3)
+    ip, ind = g.materialize()
+    assert abs(ind.numel() / g.N - 15) < 0.2  # Poisson(15) in-degrees
+    out = torch.bincount(ind, minlength=g.N).double()
+    assert abs(out.mean().item() - 15) < 0.2
+    assert out.max().item() > 5 * 15  # heavy-tailed sources
+    ip2, ind2 = SyntheticGraph(50000, 15, 1.1, seed=3).materialize()
+    assert torch.equal(ip, ip2) and torch.equal(ind, ind2)
+    ip3, ind3 = SyntheticGraph(50000, 15, 1.1, seed=4).materialize()
+    assert not torch.equal(ind, ind3)
+
+
+def test_unique_first():
+    x = torch.tensor([5, 3, 5, 9, 3, 1, 9])
+    assert unique_first(x).tolist() == [5, 3, 9, 1]
+
+
+def test_sampler_semantics_against_csc():
+    g = SyntheticGraph(20000, 15, 1.1, seed=0)
+    ip, ind = g.materialize()
+    s = NeighborSampler(g, [10, 5], seed=7)
+    seeds = seed_batches(g.N, 300, 1, 7)[0]
+    frontier = unique_first(seeds)
+    dst, src = s.sample_neighbors(frontier, 5)
+    for v in frontier[:200].tolist():
+        nb = ind[ip[v]:ip[v + 1]]
+        got = src[dst == v]
+        assert got.numel() == min(5, nb.numel())
+        # every sampled source is an in-neighbour, and multiplicities fit the edge list
+        vals, cnt = torch.unique(got, return_counts=True)
+        for a, c in zip(vals.tolist(), cnt.tolist()):
+            assert int((nb == a).sum()) >= c
+    inp, sd = s.sample(seeds)
+    assert torch.equal(inp[:seeds.numel()], unique_first(seeds))  # seeds first
+    assert torch.unique(inp).numel() == inp.numel()
+
+
+def test_sampler_is_seeded():
+    g = SyntheticGraph(10000, 15, 1.1, seed=0)
+    a = NeighborSampler(g, [15, 10, 5], seed=1000).sample(seed_batches(g.N, 64, 1, 1000)[0])[0]
+    b = NeighborSampler(g, [15, 10, 5], seed=1000).sample(seed_batches(g.N, 64, 1, 1000)[0])[0]
+    c = NeighborSampler(g, [15, 10, 5], seed=1001).sample(seed_batches(g.N, 64, 1, 1001)[0])[0]
+    assert torch.equal(a, b) and not torch.equal(a, c)
+
+
+def test_zipf_seeds_are_skewed():
+    s = seed_batches(100000, 4000, 1, 3, zipf_alpha=1.0)[0]
+    assert s.numel() == 4000 and torch.unique(s).numel() == 4000
+
+
+def test_pagerank_pin_list_matches_dense_restatement():
+    g = SyntheticGraph(15000, 15, 1.2, seed=1)
+    pins = pagerank_pin_list(g, 0.02, chunk_rows=4000)
+    ip, ind = g.materialize()
+    N = g.N
+    deg = (ip[1:] - ip[:-1]).numpy().astype(np.float64)
+    rows = np.repeat(np.arange(N), (ip[1:] - ip[:-1]).numpy())
+    src = ind.numpy()
+    pv = np.full(N, 1.0 / N)
+    for _ in range(20):  # page_rank_node_list_gen.py:126-134, zero in-degree guarded
+        norm = np.where(deg > 0, pv / np.maximum(deg, 1), 0.0)
+        new = np.zeros(N)
+        np.add.at(new, rows, norm[src])
+        pv = 0.15 / N + 0.85 * new
+    top = np.argsort(-pv, kind="stable")[: int(N * 0.02)]
+    assert set(top.tolist()) == set(pins.tolist())
+    assert pv[pins[0].item()] == pv.max()
