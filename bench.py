@@ -88,7 +88,7 @@ class Dist:
 
             import torch.distributed as dist
 
-            kw = dict(backend=backend, timeout=datetime.timedelta(seconds=600))
+            kw = dict(backend=backend, timeout=datetime.timedelta(seconds=300))
             if backend == "nccl" and device is not None:
                 kw["device_id"] = device
             dist.init_process_group(**kw)
@@ -333,7 +333,8 @@ def run_ours(args, cfg, dist: Dist):
     host_batches = [b.cpu().pin_memory() for b in batches]
     stream = torch.cuda.current_stream(device)
     bam = g.BAM_FS
-    dev_it = iter([[b] for b in batches[:args.warmup + args.steps + wb]])
+    # generators: a batch list (and the features appended to it) lives only until the step ends
+    dev_it = ([b] for b in batches[:args.warmup + args.steps + wb])
 
     # warm-up (fills the cache)
     for i in range(args.warmup):
@@ -371,7 +372,7 @@ def run_ours(args, cfg, dist: Dist):
     g.wb_init = False
     first = args.warmup + args.steps + wb
     e2e_batches = host_batches[first:first + args.steps]
-    it = iter([[b] for b in host_batches[first:]])
+    it = ([b] for b in host_batches[first:])
     if wb:  # the window of a fresh epoch is filled before the timed steps
         g.fill_wb(it, wb)
         g.wb_init = True
@@ -466,6 +467,7 @@ def run_ours(args, cfg, dist: Dist):
         "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1)},
     }
     torch.cuda.synchronize()
+    g.close()
     return result, batches
 
 
@@ -535,13 +537,20 @@ def main():
         return
 
     dist.init("nccl", torch.device("cuda", dist.local))
-    res, batches = run_ours(args, cfg, dist)
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_mmap_gather(cfg, batches, args.cpu_seconds, file_gb=args.cpu_file_gb)
-    if dist.rank == 0:
-        print(json.dumps(res), flush=True)
-    dist.barrier()
-    dist.close()
+    try:
+        res, batches = run_ours(args, cfg, dist)
+        if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_mmap_gather(cfg, batches, args.cpu_seconds, file_gb=args.cpu_file_gb)
+        if dist.rank == 0:
+            print(json.dumps(res), flush=True)
+        dist.barrier()
+    finally:
+        if dist.world > 1 and dist.rank == 0:  # the shared emulated SSD files
+            import glob
+
+            for f in glob.glob(f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd*"):
+                os.unlink(f)
+        dist.close()
 
 
 if __name__ == "__main__":

@@ -206,10 +206,15 @@ __device__ __forceinline__ void copy_segments(const SegDesc* sd, int nseg, int l
   }
 }
 
-// Whole-page copy from the backing store into a cache slot (16-byte vectors;
+// Whole-page fill from the backing store into a cache slot (16-byte vectors;
 // pages are >= 512 B, power-of-two sized, and page-aligned on both sides).
-__device__ __forceinline__ void copy_page(const char* __restrict__ src, char* __restrict__ dst, uint32_t page_size,
-                                          int lane) {
+// With FWD, the segments of the rows in `mem` (lanes whose rows read this
+// page: in-page offset `ip`, length `ln`, output `dp`, all 16-byte aligned)
+// are stored to the output from the same registers ("fill-forward"), so the
+// copy phase does not read the slot back.
+template <bool FWD>
+__device__ __forceinline__ void fill_page(const char* __restrict__ src, char* __restrict__ dst, uint32_t page_size,
+                                          int lane, unsigned mem, uint32_t ip, uint32_t ln, char* dp) {
   for (uint32_t base = 0; base < page_size; base += 32u * 16u * INFLIGHT) {
     int4 v[INFLIGHT];
 #pragma unroll
@@ -221,6 +226,21 @@ __device__ __forceinline__ void copy_page(const char* __restrict__ src, char* __
     for (int q = 0; q < INFLIGHT; q++) {
       const uint32_t off = base + ((uint32_t)q * 32u + (uint32_t)lane) * 16u;
       if (off < page_size) __stcg(reinterpret_cast<int4*>(dst + off), v[q]);
+    }
+    if (FWD) {
+      unsigned mm = mem;
+      while (mm) {
+        const int j = __ffs(mm) - 1;
+        mm &= mm - 1;
+        const uint32_t jip = __shfl_sync(0xffffffffu, ip, j);
+        const uint32_t jln = __shfl_sync(0xffffffffu, ln, j);
+        char* const jdp = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dp), j));
+#pragma unroll
+        for (int q = 0; q < INFLIGHT; q++) {
+          const uint32_t off = base + ((uint32_t)q * 32u + (uint32_t)lane) * 16u;
+          if (off >= jip && off < jip + jln) __stcs(reinterpret_cast<int4*>(jdp + (off - jip)), v[q]);
+        }
+      }
     }
   }
 }
@@ -356,6 +376,11 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       }
     }
 
+    // output row and, for cache-path lanes, the segment's place in its page
+    char* const orow = row_ok ? T.out + row * (uint64_t)a.row_bytes : nullptr;
+    const uint32_t in_pg = seg_ok ? (uint32_t)((b0 + s0) - (p << shift)) : 0u;
+    bool forwarded = false;
+
     // ---- 3. fills: per owning shard, a warp-cooperative clock sweep for
     //         victim slots (32 candidates per atomic on that shard's hand)
     unsigned pending = __ballot_sync(0xffffffffu, cls == CLS_OWN);
@@ -424,7 +449,15 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         const unsigned long long po = __shfl_sync(0xffffffffu, (unsigned long long)p, o);
         const unsigned long long so = __shfl_sync(0xffffffffu, (unsigned long long)slot, o);
         const uint32_t ow = __shfl_sync(0xffffffffu, owner, o);
-        copy_page(backing_addr(a.b, po, shift), a.c.sh[ow].slots + (so << shift), a.c.page_size, lane);
+        const unsigned mem = __shfl_sync(0xffffffffu, eq, o);  // lanes whose rows read page po
+        if (VEC == 16) {
+          fill_page<true>(backing_addr(a.b, po, shift), a.c.sh[ow].slots + (so << shift), a.c.page_size, lane, mem,
+                          in_pg, s1 - s0, orow + s0);
+          if ((mem >> lane) & 1u) forwarded = true;
+        } else {
+          fill_page<false>(backing_addr(a.b, po, shift), a.c.sh[ow].slots + (so << shift), a.c.page_size, lane,
+                           0u, 0u, 0u, nullptr);
+        }
         __syncwarp();
         if (lane == o) {
           // the release reduction orders the warp's slot stores (made visible
@@ -464,7 +497,6 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const char* src = nullptr;
     char* dst = nullptr;
     uint32_t len = 0;
-    char* const orow = row_ok ? T.out + row * (uint64_t)a.row_bytes : nullptr;
     if (bad && sidx == 0) {
       len = a.row_bytes;  // zero row
       dst = orow;
@@ -472,12 +504,11 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       src = a.cpu.buf + cpu_slot * a.cpu.stride;
       dst = orow;
       len = a.row_bytes;
-    } else if (seg_ok) {
-      const uint64_t in_page = (b0 + s0) - (p << shift);
+    } else if (seg_ok && !forwarded) {
       if (gcls == CLS_BYPASS)
-        src = backing_addr(a.b, p, shift) + in_page;
+        src = backing_addr(a.b, p, shift) + in_pg;
       else
-        src = S.slots + (gslot << shift) + in_page;
+        src = S.slots + (gslot << shift) + in_pg;
       dst = orow + s0;
       len = s1 - s0;
     }
@@ -506,11 +537,13 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const unsigned n_hit = __popc(__ballot_sync(0xffffffffu, seg_ok && gcls == CLS_HIT));
     const unsigned n_miss = __popc(__ballot_sync(0xffffffffu, seg_ok && (gcls == CLS_OWN || gcls == CLS_WAITED)));
     const unsigned n_byp = __popc(__ballot_sync(0xffffffffu, seg_ok && gcls == CLS_BYPASS));
-    const unsigned lh = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_HIT ? len : 0u);
-    const unsigned lm = __reduce_add_sync(0xffffffffu, seg_ok && (gcls == CLS_OWN || gcls == CLS_WAITED) ? len : 0u);
-    const unsigned lb = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_BYPASS ? len : 0u);
+    const unsigned sl = seg_ok ? s1 - s0 : 0u;  // segment bytes, copied or forwarded
+    const unsigned lh = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_HIT ? sl : 0u);
+    const unsigned lm = __reduce_add_sync(0xffffffffu, seg_ok && (gcls == CLS_OWN || gcls == CLS_WAITED) ? sl : 0u);
+    const unsigned lb = __reduce_add_sync(0xffffffffu, seg_ok && gcls == CLS_BYPASS ? sl : 0u);
     const unsigned lc = __reduce_add_sync(0xffffffffu, pinned && r0 ? len : 0u);
-    const unsigned lpeer = SYS ? __reduce_add_sync(0xffffffffu, cached && owner != a.c.rank ? len : 0u) : 0u;
+    const unsigned lpeer = SYS ? __reduce_add_sync(0xffffffffu, cached && owner != a.c.rank && !forwarded ? sl : 0u)
+                               : 0u;
     if (lane == 0) {
       acc[K_ROWS] += n_rows_c;
       acc[K_CPU] += n_cpu;

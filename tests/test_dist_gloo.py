@@ -1,0 +1,95 @@
+"""Multi-rank host logic on CPU (gloo, world size 2): the bench's
+max/sum-over-ranks timing helpers, per-rank sampler seeds, and the CUDA IPC
+handle exchange of a sharded GIDS (with a fake store recording what it got)."""
+import os
+import sys
+
+import pytest
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+
+
+def _worker(rank, world, port, q):
+    try:
+        for p in (REPO, os.path.join(REPO, "gids-study_b200"), HERE):
+            sys.path.insert(0, p)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                          LOCAL_RANK=str(rank))
+        import bench
+
+        d = bench.Dist()
+        d.init("gloo")
+        t_max = d.max(1.0 + rank)
+        s_sum = d.sum(10.0 * (rank + 1))
+        d.barrier()
+
+        # sharded GIDS handle exchange with a fake store
+        import torch
+
+        gmod = sys.modules["GIDS.GIDS"] if "GIDS.GIDS" in sys.modules else None
+        import GIDS  # noqa: F401
+
+        gmod = sys.modules["GIDS.GIDS"]
+
+        class FakeCtrl:
+            def init_GIDS_controllers(self, *a):
+                pass
+
+            def set_emulation(self, *a):
+                pass
+
+        class FakeStore:
+            def __init__(self):
+                self.calls = []
+
+            def __getattr__(self, name):
+                def rec(*a):
+                    self.calls.append((name,) + a)
+
+                return rec
+
+            def ipc_handle(self):
+                return bytes([rank]) * 64
+
+            def open_peers(self, handles):
+                self.calls.append(("open_peers", list(handles)))
+
+        gmod._STORE_CLASSES = {torch.float32: FakeStore}
+        gmod.BAM_Feature_Store.GIDS_Controllers = FakeCtrl
+        g = gmod.GIDS(page_size=4096, cache_dim=64, num_ele=1000 * 64, shard_cache=True)
+        names = [c[0] for c in g.BAM_FS.calls]
+        opened = [c for c in g.BAM_FS.calls if c[0] == "open_peers"][0][1]
+        q.put((rank, t_max, s_sum, bench.sampler_seed(rank), g.world, g.rank, names, opened))
+        d.close()
+    except Exception as e:
+        q.put((rank, "error", repr(e)))
+
+
+def test_two_ranks_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 200
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    try:
+        for _ in range(2):
+            r = q.get(timeout=180)
+            out[r[0]] = r
+    finally:
+        for p in ps:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for r in (0, 1):
+        assert out[r][1] != "error", out[r]
+        _, t_max, s_sum, seed, world, grank, names, opened = out[r]
+        assert t_max == 2.0 and s_sum == 30.0  # max and sum over both ranks
+        assert seed == 1000 + r
+        assert (world, grank) == (2, r)
+        # sharding is set before init_controllers; handles arrive in rank order
+        assert names.index("set_sharding") < names.index("init_controllers") < names.index("open_peers")
+        assert opened == [bytes([0]) * 64, bytes([1]) * 64]
