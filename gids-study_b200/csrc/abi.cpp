@@ -17,6 +17,8 @@ struct gids_store {
   gids::Store s;
 };
 
+gids::Store* gids_store_of(gids_store_t* s) { return &s->s; }
+
 namespace gids {
 namespace {
 thread_local std::string g_last_error;

@@ -220,6 +220,9 @@ class Store {
   void cpu_backing_buffer(uint64_t dim, uint64_t len);
   void set_cpu_buffer(const int64_t* host_idx, int64_t num);
   void set_row_layout(uint32_t cache_dim);
+  // gather with the page cache in the library's static no-allocation scratch (noalloc.cu)
+  void read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
+                    cudaStream_t st);
   void store_tensor(const void* src, uint64_t num_rows, uint64_t offset_bytes);
   void write_range(const void* src, uint64_t nbytes, uint64_t off);
   void flush_cache();
@@ -299,3 +302,6 @@ class Store {
 };
 
 }  // namespace gids
+
+// The Store behind a C handle (abi.cpp).
+gids::Store* gids_store_of(gids_store_t* s);

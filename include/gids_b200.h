@@ -151,6 +151,25 @@ GIDS_API int gids_read_feature(gids_store_t *s, void *out, const int64_t *idx, i
 GIDS_API int gids_read_feature_multi(gids_store_t *s, int k, void *const *outs, const int64_t *const *idxs,
                             const uint64_t *ns, int dim, int cache_dim, const uint64_t *key_offs, void *stream);
 
+/* No counterpart in the reference. The same gather as gids_read_feature, for
+ * callers that cannot allocate GPU memory -- for example a process whose
+ * device memory belongs to another allocator with a hard budget (a serving
+ * runtime, or a framework caching allocator that reserved the GPU), where a
+ * cudaMalloc fails or takes memory promised elsewhere. It allocates nothing:
+ * the page cache its kernel uses (page table, slots, counters) lives in a
+ * 32 MiB static device array that every GPU loading this library holds until
+ * the process exits; the store's own cache is neither read nor written. The
+ * store must already be initialised (by a caller that could allocate).
+ * Each call starts from an empty cache (it clears the page table, tags and
+ * counters on its stream), so pages shared by rows of one call are fetched
+ * once and nothing carries over between calls. The first call on a device
+ * looks the array's address up; make it before any stream capture. All calls
+ * on a device share the array: calls that overlap on the GPU race. A store
+ * whose range needs more than about 4M pages of page table gets
+ * GIDS_E_RANGE. */
+GIDS_API int gids_read_feature_noalloc(gids_store_t *s, void *out, const int64_t *idx, int64_t n, int dim,
+                                       int cache_dim, uint64_t key_off, void *stream);
+
 /* ---------------------------------------------------- window buffering --
  * Replaces set_window_buffering (gids_nvme.cu:242-249; kernel
  * gids_kernel.cu:246-256): marks the pages of the rows (idx[i] + hash_off)

@@ -48,6 +48,7 @@ def lib():
             "gids_store_set_row_layout": (i32, [vp, u32]),
             "gids_read_feature": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
             "gids_read_feature_multi": (i32, [vp, i32, P(vp), P(vp), P(u64), i32, i32, P(u64), vp]),
+            "gids_read_feature_noalloc": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
             "gids_set_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_cpu_backing_buffer": (i32, [vp, u64, u64]),
             "gids_set_cpu_buffer": (i32, [vp, vp, i32]),
