@@ -51,7 +51,9 @@ for _p in (REPO, PKG):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-BASE = dict(cpu_pin_frac=0.0, wb=0, phys_gb=64.0)
+BASE = dict(cpu_pin_frac=0.0, wb=0, phys_gb=64.0, line=0, hetero=None)
+C3_TYPES = {"t0": 40_000_000, "t1": 30_000_000, "t2": 5_000_000, "t3": 1_000_000}
+C3_RELATIONS = [("t0", "t0"), ("t1", "t0"), ("t2", "t0"), ("t3", "t0"), ("t0", "t1"), ("t1", "t2")]
 CONFIGS = {
     # nodes, mean degree, zipf alpha of the out-degree, feature dim/dtype, page size, emulated SSDs,
     # cache MB per GPU, fanouts, seed batch, seed law (None = uniform), pinned fraction, WB depth
@@ -59,11 +61,14 @@ CONFIGS = {
                cache_mb=4096, fanouts=[10, 5], batch=1024, seed_zipf=None),
     "c2": dict(BASE, nodes=100_000_000, mean_deg=15, alpha=1.1, dim=1024, dtype="float32", page=4096, ssds=4,
                cache_mb=40 * 1024, fanouts=[15, 10, 5], batch=4096, seed_zipf=None),
+    "c3": dict(BASE, nodes=sum(C3_TYPES.values()), mean_deg=8, alpha=1.0, dim=1024, dtype="float32", page=4096,
+               ssds=4, cache_mb=40 * 1024, fanouts=[15, 10], batch=1024, seed_zipf=None,
+               hetero=dict(types=C3_TYPES, relations=C3_RELATIONS, seed_type="t0")),
     "c4": dict(BASE, nodes=50_000_000, mean_deg=15, alpha=1.2, dim=768, dtype="float16", page=4096, ssds=4,
                cache_mb=8 * 1024, fanouts=[10, 10], batch=2048, seed_zipf=1.0, cpu_pin_frac=0.01, wb=8,
-               phys_gb=80.0),
+               phys_gb=80.0, line=512),
     "c5": dict(BASE, nodes=500_000_000, mean_deg=10, alpha=1.1, dim=128, dtype="float32", page=4096, ssds=8,
-               cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None),
+               cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None, line=512),
 }
 KIND = {"float32": 1, "float16": 2}
 TDTYPE = {"float32": torch.float32, "float16": torch.float16}
@@ -187,6 +192,18 @@ def make_batches(cfg, n_batches, rank, device, with_pins=False):
     from GIDS.synthetic import NeighborSampler, SyntheticGraph, pagerank_pin_list, seed_batches
 
     t0 = time.time()
+    if cfg["hetero"]:
+        from GIDS.synthetic import HeteroNeighborSampler, HeteroSyntheticGraph
+
+        h = cfg["hetero"]
+        hg = HeteroSyntheticGraph(h["types"], h["relations"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
+        hs = HeteroNeighborSampler(hg, cfg["fanouts"], seed=sampler_seed(rank))
+        seeds = seed_batches(h["types"][h["seed_type"]], cfg["batch"], n_batches, sampler_seed(rank), device=device)
+        out = [hs.sample({h["seed_type"]: sd})[0] for sd in seeds]
+        del hg, hs
+        if device != "cpu":
+            torch.cuda.synchronize()
+        return (out, None, time.time() - t0) if with_pins else (out, time.time() - t0)
     g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
     pins = None
     if with_pins and cfg["cpu_pin_frac"] > 0:
@@ -250,11 +267,20 @@ def cpu_mmap_gather(cfg, ids_list, seconds_budget, path_dir="/dev/shm", file_gb=
     del mm
     feat = oracle.open_memmap_table(path, np.dtype(dt), rows, dim)
     try:
+        def flat(ids):
+            if isinstance(ids, dict):  # heterograph: type-local ids + the type's offset
+                offs, acc = {}, 0
+                for t, n in cfg["hetero"]["types"].items():
+                    offs[t] = acc
+                    acc += n
+                return np.concatenate([v.cpu().numpy() + offs[k] for k, v in ids.items()])
+            return ids.cpu().numpy()
+
         for ids in warmup_ids:
-            oracle.mmap_index_select(feat, torch.as_tensor(ids.cpu().numpy() % rows))
+            oracle.mmap_index_select(feat, torch.as_tensor(flat(ids) % rows))
         done_rows, t_total, n_batches = 0, 0.0, 0
         for ids in ids_list:
-            ids_m = torch.as_tensor(ids.cpu().numpy() % rows)
+            ids_m = torch.as_tensor(flat(ids) % rows)
             t0 = time.perf_counter()
             out = oracle.mmap_index_select(feat, ids_m)
             t_total += time.perf_counter() - t0
@@ -287,6 +313,12 @@ def run_ours(args, cfg, dist: Dist):
     phys = min(int(cfg["phys_gb"] * 1e9), range_bytes)
     per_ssd = (phys // cfg["ssds"]) // page * page
     shared = dist.world > 1
+    hmap = None
+    if cfg["hetero"]:
+        hmap, acc = {}, 0
+        for t, n in cfg["hetero"]["types"].items():
+            hmap[t] = acc
+            acc += n
     pattern = f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd{{}}" if shared else None
 
     t0 = time.time()
@@ -309,7 +341,8 @@ def run_ours(args, cfg, dist: Dist):
                   ssd_list=list(range(cfg["ssds"])), cache_size=cfg["cache_mb"], ctrl_idx=dist.local,
                   dtype=TDTYPE[dt], ssd_capacity=per_ssd if phys < range_bytes else 0, ssd_path=pattern,
                   synchronous=False, shard_cache=shared and not args.no_shard, window_buffer=cfg["wb"] > 0,
-                  wb_size=max(1, cfg["wb"]))
+                  wb_size=max(1, cfg["wb"]), cache_line=cfg["line"] or None,
+                  heterograph=cfg["hetero"] is not None, heterograph_map=hmap)
     t_store = time.time() - t0
     if not shared:
         t0 = time.time()
@@ -322,7 +355,14 @@ def run_ours(args, cfg, dist: Dist):
     # each timed loop consumes `steps` batches; window buffering reads wb batches ahead
     n_batches = args.warmup + 2 * (args.steps + wb)
     batches, pins, t_sample = make_batches(cfg, n_batches, dist.rank, device, with_pins=True)
-    sizes = [int(b.numel()) for b in batches]
+
+    def nrows(b):
+        return sum(int(v.numel()) for v in b.values()) if isinstance(b, dict) else int(b.numel())
+
+    def pin(b):
+        return {k: v.cpu().pin_memory() for k, v in b.items()} if isinstance(b, dict) else b.cpu().pin_memory()
+
+    sizes = [nrows(b) for b in batches]
     log(f"[rank {dist.rank}] sampled {n_batches} minibatches in {t_sample:.1f}s, input nodes mean "
         f"{np.mean(sizes):.0f}")
     if pins is not None:
@@ -330,7 +370,7 @@ def run_ours(args, cfg, dist: Dist):
         g.set_cpu_buffer(pins, int(pins.numel()))
         log(f"[rank {dist.rank}] constant CPU buffer: {pins.numel()} pinned rows (PageRank top "
             f"{cfg['cpu_pin_frac']:.0%})")
-    host_batches = [b.cpu().pin_memory() for b in batches]
+    host_batches = [pin(b) for b in batches]
     stream = torch.cuda.current_stream(device)
     bam = g.BAM_FS
     # generators: a batch list (and the features appended to it) lives only until the step ends
@@ -387,7 +427,10 @@ def run_ours(args, cfg, dist: Dist):
     checks = 0.0
     for _ in e2e_batches:
         batch = g.fetch_feature(dim, it, device)
-        checks += float(batch[-1][-1, -1].item())  # D2H read of the step's result
+        feat = batch[-1]
+        if isinstance(feat, dict):
+            feat = feat[max(feat, key=lambda k: feat[k].shape[0])]
+        checks += float(feat[-1, -1].item())  # D2H read of the step's result
     e1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -444,21 +487,21 @@ def run_ours(args, cfg, dist: Dist):
         "data": "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)",
         "minibatches_per_s": round(steps_all / t_val_max, 3),
         "config": {"workload": f"{args.config}: {cfg['nodes']} nodes, {dt} x {dim} ({range_bytes / 1e9:.1f} GB range), "
-                               f"{page} B pages over {cfg['ssds']} emulated SSDs, {cfg['cache_mb'] // 1024} GB cache/GPU, "
-                               f"fanout {cfg['fanouts']}, batch {cfg['batch']}",
+                               f"{page} B pages over {cfg['ssds']} emulated SSDs, {cfg['cache_mb'] // 1024} GB cache/GPU "
+                               f"in {geo.get('cache_line', page)} B lines, fanout {cfg['fanouts']}, batch {cfg['batch']}",
                    "global_batch": cfg["batch"] * dist.world,
                    "parallelism": f"dp{dist.world} (independent trainers" +
                                   (", page cache sharded by page id over NVLink)" if g.world > 1 else ")"),
                    "backing_store": {"logical_bytes": range_bytes, "physical_bytes": geo["wrap_pages"] * page,
                                      "wrap_pages": geo["wrap_pages"]},
                    "l2": (f"no flush: every step reads {min(sizes) * row_bytes / 1e9:.2f} GB or more (L2 is 126 MB)"
-                          if min(sizes) * row_bytes > 4 * 126e6 else "steps smaller than 4x L2: not a timing run"),
+                          if min(sizes) * row_bytes > 126e6 else "steps smaller than L2: not a timing run"),
                    "input_nodes_per_step": round(rows_val / max(1, len(dev_ids)), 1),
                    "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
                    "window_buffer_depth": wb},
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "api": "GIDS.fetch_feature",
-                "h2d_bytes_per_step": int(np.mean([b.numel() * 8 for b in e2e_batches])),
+                "h2d_bytes_per_step": int(np.mean([nrows(b) * 8 for b in e2e_batches])),
                 "d2h_bytes_per_step": esize, "wall_s": round(wall_e2e, 3),
                 "minibatches_per_s": round(dist.sum(len(e2e_batches)) / t_e2e_max, 3),
                 "mix": {"hit": round(st_e2e["hit"] / max(1, st_e2e["access"]), 4)}},
@@ -478,7 +521,7 @@ def run_reference(args, cfg, dist: Dist):
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     n = args.warmup + args.steps
     batches, _ = make_batches(cfg, n, 0, dev)
-    batches = [b.cpu() for b in batches]
+    batches = [{k: v.cpu() for k, v in b.items()} if isinstance(b, dict) else b.cpu() for b in batches]
     dt, dim = cfg["dtype"], cfg["dim"]
     row_bytes = dim * ESIZE[dt]
     # each step is one whole minibatch gathered by torch.index_select from the memmap
@@ -513,6 +556,7 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override the seed batch size (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-shard", action="store_true", help="N>1: independent caches instead of one sharded cache")
+    ap.add_argument("--cache-line", type=int, default=-1, help="cache line bytes (0 = the page; -1 = the config's)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3")
@@ -526,6 +570,8 @@ def main():
         cfg["batch"] = args.batch
     if args.phys_gb:
         cfg["phys_gb"] = args.phys_gb
+    if args.cache_line >= 0:
+        cfg["line"] = args.cache_line
 
     dist = Dist()
     if args.impl == "reference":

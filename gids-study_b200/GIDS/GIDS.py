@@ -69,13 +69,16 @@ class GIDS:
     (one process per GPU), the ranks' page caches form one cache sharded by
     page id (page p lives on rank p % world) and hits on other ranks' pages
     are read over NVLink. Every rank must construct its GIDS collectively
-    with the same geometry, and call ``close()`` collectively.
+    with the same geometry, and call ``close()`` collectively. ``cache_line``
+    (bytes, a power of two in [512, page_size]; default the page) sets the
+    unit the GPU cache holds and fetches, so that rows much smaller than a
+    page do not pull whole pages over the host link.
     """
 
     def __init__(self, page_size=4096, off=0, cache_dim=1024, num_ele=300 * 1000 * 1000 * 1024, num_ssd=1,
                  ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
                  long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
-                 ssd_path=None, synchronous=False, shard_cache=False, process_group=None):
+                 ssd_path=None, synchronous=False, shard_cache=False, process_group=None, cache_line=None):
         if dtype is None:
             dtype = torch.int64 if long_type else torch.float32
         if dtype not in _STORE_CLASSES:
@@ -118,6 +121,8 @@ class GIDS:
             self.GIDS_controller.set_emulation(int(ssd_capacity or 0), ssd_path or "")
 
         self.BAM_FS.set_device(ctrl_idx)
+        if cache_line:
+            self.BAM_FS.set_cache_line(int(cache_line))
         self._pg = None
         self.world, self.rank = 1, 0
         if shard_cache:

@@ -256,3 +256,59 @@ def pagerank_pin_list(graph: SyntheticGraph, fraction: float = 0.01, damping: fl
         pv = (1.0 - damping) / N + damping * new
     k = max(1, int(N * fraction))
     return torch.topk(pv, k, largest=True).indices
+
+
+class HeteroSyntheticGraph:
+    """Heterograph of several node types; every relation (src type, dst type)
+    is a SyntheticGraph over the source type: Poisson(mean) in-edges per
+    destination node, sources drawn proportionally to truncated-Zipf weights."""
+
+    def __init__(self, type_sizes: dict, relations, mean_degree: float = 8.0, alpha: float = 1.0, seed: int = 0,
+                 device="cpu"):
+        self.type_sizes = dict(type_sizes)
+        self.relations = [tuple(r) for r in relations]
+        self.device = torch.device(device)
+        self.rel = {}
+        for i, (src, dst) in enumerate(self.relations):
+            self.rel[(src, dst)] = SyntheticGraph(self.type_sizes[src], mean_degree, alpha, seed=seed * 100 + i + 1,
+                                                  device=device)
+
+    def offsets(self) -> dict:
+        """heterograph_map: first global node id of each type (types laid out in order)."""
+        out, acc = {}, 0
+        for t, n in self.type_sizes.items():
+            out[t] = acc
+            acc += n
+        return out
+
+
+class HeteroNeighborSampler:
+    """Seeded stand-in for DGL's MultiLayerNeighborSampler on a heterograph:
+    every hop samples min(fanout, in_degree) in-edges per frontier node along
+    every relation whose destination type the node has."""
+
+    def __init__(self, graph: HeteroSyntheticGraph, fanouts, seed: int = 1000):
+        self.g = graph
+        self.fanouts = [int(f) for f in fanouts]
+        self.samplers = {r: NeighborSampler(g, [1], seed=seed + 7 * i) for i, (r, g) in enumerate(graph.rel.items())}
+
+    def sample(self, seeds: dict):
+        """{type: input node ids (type-local ids, seeds first)}, seeds."""
+        dev = self.g.device
+        nodes = {t: torch.zeros(0, dtype=torch.int64, device=dev) for t in self.g.type_sizes}
+        for t, s in seeds.items():
+            nodes[t] = unique_first(s.to(dev))
+        for f in reversed(self.fanouts):
+            new = {t: [] for t in nodes}
+            for (src, dst), smp in self.samplers.items():
+                if nodes[dst].numel() == 0:
+                    continue
+                _, nb = smp.sample_neighbors(nodes[dst], f)
+                new[src].append(nb)
+            for t, parts in new.items():
+                if not parts:
+                    continue
+                cand = unique_first(torch.cat(parts))
+                cand = cand[~torch.isin(cand, nodes[t])]
+                nodes[t] = torch.cat([nodes[t], cand])
+        return nodes, seeds

@@ -189,6 +189,13 @@ int gids_store_set_synchronous(gids_store_t* s, int sync) {
   });
 }
 
+int gids_store_set_cache_line(gids_store_t* s, uint32_t bytes) {
+  return guarded([&] {
+    NEED(s);
+    s->s.set_cache_line(bytes);
+  });
+}
+
 int gids_store_set_row_layout(gids_store_t* s, uint32_t cache_dim) {
   return guarded([&] {
     NEED(s);
@@ -400,9 +407,10 @@ int gids_store_geometry(gids_store_t* s, uint64_t* out, int count) {
     NEED(s);
     NEED(out);
     GIDS_CHECK(s->s.initialized, GIDS_E_STATE, "geometry before init_controllers");
-    const uint64_t g[6] = {s->s.n_pages,       s->s.ctrls->wrap_pages, s->s.ctrls->ssd.empty() ? 0 : s->s.ctrls->ssd[0].bytes,
-                           s->s.n_slots,       s->s.page_size,         s->s.ctrls->n_bound};
-    for (int i = 0; i < count && i < 6; i++) out[i] = g[i];
+    const uint64_t g[7] = {s->s.n_pages, s->s.ctrls->wrap_pages, s->s.ctrls->ssd.empty() ? 0 : s->s.ctrls->ssd[0].bytes,
+                           s->s.n_slots, s->s.page_size,         s->s.ctrls->n_bound,
+                           s->s.line_size};
+    for (int i = 0; i < count && i < 7; i++) out[i] = g[i];
   });
 }
 

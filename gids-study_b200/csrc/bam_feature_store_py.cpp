@@ -92,6 +92,7 @@ class FeatureStore {
     check(gids_store_create(&s, eb_, dev));
     int rc = GIDS_OK;
     if (world_ > 1) rc = gids_store_set_sharding(s, world_, rank_);
+    if (rc == GIDS_OK && line_) rc = gids_store_set_cache_line(s, line_);
     if (rc == GIDS_OK) rc = gids_store_init_controllers(s, ctrl.c, ps, read_off, cache_size, num_ele, num_ssd);
     if (rc != GIDS_OK) {
       char buf[1024];
@@ -180,6 +181,11 @@ class FeatureStore {
     world_ = world;
     rank_ = rank;
   }
+  // cache line in bytes (must be set before init_controllers; 0 = the page)
+  void set_cache_line(uint32_t bytes) {
+    if (s_) throw std::runtime_error("gids: set_cache_line after init_controllers");
+    line_ = bytes;
+  }
   py::bytes ipc_handle() {
     char h[64];
     check(gids_store_ipc_handle(s(), h, sizeof(h)));
@@ -225,8 +231,8 @@ class FeatureStore {
     check(gids_read_range_host(s(), (void*)dst, nbytes, offset));
   }
   py::dict geometry() {
-    uint64_t g[6] = {0};
-    check(gids_store_geometry(s(), g, 6));
+    uint64_t g[7] = {0};
+    check(gids_store_geometry(s(), g, 7));
     py::dict d;
     d["range_pages"] = g[0];
     d["wrap_pages"] = g[1];
@@ -234,6 +240,7 @@ class FeatureStore {
     d["cache_slots"] = g[3];
     d["page_size"] = g[4];
     d["num_ssd"] = g[5];
+    d["cache_line"] = g[6];
     return d;
   }
   uint32_t elem_bytes() const { return eb_; }
@@ -248,6 +255,7 @@ class FeatureStore {
   uint32_t eb_;
   int device_ = -1;
   int world_ = 1, rank_ = 0;
+  uint32_t line_ = 0;
   uint32_t page_size_ = 0;
   gids_store_t* s_ = nullptr;
   std::vector<uint64_t> offsets_{0, 0, 0};
@@ -298,6 +306,7 @@ void bind_store(py::module_& m, const char* name) {
       // extensions
       .def("set_device", &S::set_device)
       .def("set_sharding", &S::set_sharding, py::arg("world"), py::arg("rank"))
+      .def("set_cache_line", &S::set_cache_line, py::arg("bytes"))
       .def("ipc_handle", &S::ipc_handle)
       .def("open_peers", &S::open_peers)
       .def("set_synchronous", &S::set_synchronous, R())

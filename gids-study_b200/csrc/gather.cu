@@ -245,13 +245,15 @@ __device__ __forceinline__ void fill_page(const char* __restrict__ src, char* __
   }
 }
 
-// Address of logical page p on the emulated SSDs (page_cache_backup.h:626-652,
-// STRIPE): SSD p % n, device page page_start + p / n, after the wrap.
-__device__ __forceinline__ const char* backing_addr(const DevBacking& b, uint64_t p, uint32_t shift) {
+// Address of cache line l on the emulated SSDs: its stripe page p (after the
+// wrap) lives on SSD p % n at device page page_start + p / n
+// (page_cache_backup.h:626-652, STRIPE); the line sits at its offset in p.
+__device__ __forceinline__ const char* backing_addr(const DevBacking& b, uint64_t l, uint32_t line_shift) {
+  const uint64_t p = l >> b.lpp_shift;
   const uint64_t q = p % b.wrap_pages;
   const uint32_t c = (uint32_t)(q % b.n_ssd);
   const uint64_t dp = b.page_start + q / b.n_ssd;
-  return b.ssd[c] + (dp << shift);
+  return b.ssd[c] + (dp << b.page_shift) + ((l & ((1ull << b.lpp_shift) - 1ull)) << line_shift);
 }
 
 // Saturating decrement of a window-buffer pin counter (bounded CAS loop).
@@ -280,6 +282,7 @@ template <int VEC, bool SYS>
 __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_constant__ GatherArgs a) {
   __shared__ SegDesc seg_sh[WARPS][32];
   __shared__ unsigned long long cnt_sh[WARPS][K_N];  // warp-private counters
+  __shared__ unsigned char fill_lane[WARPS][8];      // owner lanes of one fill batch
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   SegDesc* sd = seg_sh[wib];
@@ -443,13 +446,91 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         cls = CLS_BYPASS;
       }
       unsigned fills = __ballot_sync(0xffffffffu, cls == CLS_OWN);
-      while (fills) {
+      if (shift <= 12) {
+        // Lines of at most 4 KB: one 4 KB block of 8 vectors per lane covers
+        // 8 >> (shift - 9) lines, so that many fills share one round trip over
+        // the host link. Vector q of every lane belongs to line q >> (shift - 9)
+        // of the batch: warp-uniform, so owners are broadcast reads.
+        const uint32_t qsh = shift - 9;
+        const int per_batch = 8 >> qsh;
+        unsigned char* const bl = fill_lane[wib];
+        while (fills) {
+          int nb = 0;
+          if (lane == 0) {
+            unsigned f = fills;
+            for (; nb < per_batch && f; nb++) {
+              bl[nb] = (unsigned char)(__ffs(f) - 1);
+              f &= f - 1;
+            }
+          }
+          nb = __shfl_sync(0xffffffffu, nb, 0);
+          __syncwarp();
+          unsigned batch = 0;
+          for (int j = 0; j < nb; j++) batch |= 1u << bl[j];
+          fills &= ~batch;
+          const uint32_t qmask = (1u << qsh) - 1u;
+          int4 v[INFLIGHT];
+          const char* sq = nullptr;
+#pragma unroll
+          for (int q = 0; q < INFLIGHT; q++) {
+            const int j = q >> qsh;
+            if (j < nb) {
+              if (((uint32_t)q & qmask) == 0) {  // first vector of line j: its source address
+                const unsigned long long po = __shfl_sync(0xffffffffu, (unsigned long long)p, bl[j]);
+                sq = backing_addr(a.b, po, shift);
+              }
+              const uint32_t off = (((uint32_t)q << 9) + ((uint32_t)lane << 4)) & (a.c.page_size - 1u);
+              v[q] = __ldcg(reinterpret_cast<const int4*>(sq + off));
+            }
+          }
+          char* dq = nullptr;
+          unsigned mm = 0;
+#pragma unroll
+          for (int q = 0; q < INFLIGHT; q++) {
+            const int j = q >> qsh;
+            if (j < nb) {
+              if (((uint32_t)q & qmask) == 0) {  // first vector of line j: its slot and readers
+                const int o = bl[j];
+                const unsigned long long so = __shfl_sync(0xffffffffu, (unsigned long long)slot, o);
+                const uint32_t ow = __shfl_sync(0xffffffffu, owner, o);
+                dq = a.c.sh[ow].slots + (so << shift);
+                mm = __shfl_sync(0xffffffffu, eq, o);  // lanes whose rows read line j
+                if (VEC == 16 && ((mm >> lane) & 1u)) forwarded = true;
+              }
+              const uint32_t off = (((uint32_t)q << 9) + ((uint32_t)lane << 4)) & (a.c.page_size - 1u);
+              __stcg(reinterpret_cast<int4*>(dq + off), v[q]);
+              if (VEC == 16) {  // fill-forward: the rows of line j straight from registers
+                unsigned rest = mm;
+                while (rest) {
+                  const int m = __ffs(rest) - 1;
+                  rest &= rest - 1;
+                  const uint32_t jip = __shfl_sync(0xffffffffu, in_pg, m);
+                  const uint32_t jln = __shfl_sync(0xffffffffu, s1 - s0, m);
+                  const unsigned long long jdp =
+                      __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow + s0), m);
+                  if (off >= jip && off < jip + jln)
+                    __stcs(reinterpret_cast<int4*>(reinterpret_cast<char*>(jdp) + (off - jip)), v[q]);
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if ((batch >> lane) & 1u) {
+            // the release reduction orders the warp's slot stores (made visible
+            // to this lane by __syncwarp) before the VALID bit
+            red_add_release<SYS>(stw, ((unsigned long long)slot << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
+            atomicAdd(acc + K_READIO, 1ull);
+          }
+          __syncwarp();
+        }
+      }
+      while (fills) {  // lines larger than 4 KB: one fill at a time, 4 KB blocks
         const int o = __ffs(fills) - 1;
         fills &= fills - 1;
         const unsigned long long po = __shfl_sync(0xffffffffu, (unsigned long long)p, o);
         const unsigned long long so = __shfl_sync(0xffffffffu, (unsigned long long)slot, o);
         const uint32_t ow = __shfl_sync(0xffffffffu, owner, o);
-        const unsigned mem = __shfl_sync(0xffffffffu, eq, o);  // lanes whose rows read page po
+        const unsigned mem = __shfl_sync(0xffffffffu, eq, o);  // lanes whose rows read line po
         if (VEC == 16) {
           fill_page<true>(backing_addr(a.b, po, shift), a.c.sh[ow].slots + (so << shift), a.c.page_size, lane, mem,
                           in_pg, s1 - s0, orow + s0);
@@ -460,8 +541,6 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         }
         __syncwarp();
         if (lane == o) {
-          // the release reduction orders the warp's slot stores (made visible
-          // to this lane by __syncwarp) before the VALID bit
           red_add_release<SYS>(stw, (so << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
           acc[K_READIO]++;  // only lane o touches it here
         }

@@ -82,12 +82,16 @@ struct DevShard {
   unsigned long long* clock;      // clock hand
 };
 
+// The cache works in lines: a line is the unit of the page table, of a slot
+// and of a fill. It divides the stripe page of the backing store (by default
+// it is the page, as in the reference; smaller lines stop small rows from
+// pulling whole pages over the host link).
 struct DevCache {
   DevShard sh[GIDS_MAX_WORLD];
   uint64_t n_slots;  // slots per shard
-  uint64_t n_pages;  // pages of the whole range
-  uint32_t page_shift;
-  uint32_t page_size;
+  uint64_t n_pages;  // lines of the whole range
+  uint32_t page_shift;  // log2(line size)
+  uint32_t page_size;   // line size in bytes
   uint32_t world;  // ranks sharing the cache (1 = unsharded)
   uint32_t rank;
 };
@@ -97,6 +101,8 @@ struct DevBacking {
   uint32_t n_ssd;
   uint64_t page_start;  // first page of the range on every SSD
   uint64_t wrap_pages;  // pages physically held (== n_pages when the SSDs hold the whole range)
+  uint32_t page_shift;  // log2(stripe page size)
+  uint32_t lpp_shift;   // log2(cache lines per stripe page)
 };
 
 struct DevCpuBuf {
@@ -220,6 +226,7 @@ class Store {
   void cpu_backing_buffer(uint64_t dim, uint64_t len);
   void set_cpu_buffer(const int64_t* host_idx, int64_t num);
   void set_row_layout(uint32_t cache_dim);
+  void set_cache_line(uint32_t bytes);
   // gather with the page cache in the library's static no-allocation scratch (noalloc.cu)
   void read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
                     cudaStream_t st);
@@ -239,13 +246,15 @@ class Store {
   bool synchronous = true;
   Controllers* ctrls = nullptr;
   bool initialized = false;
-  uint32_t page_size = 0, page_shift = 0;
+  uint32_t page_size = 0, page_shift = 0;   // stripe page of the backing store
+  uint32_t line_size = 0, line_shift = 0;   // cache line (divides the page)
+  uint32_t line_request = 0;                // set_cache_line before init; 0 = the page
   uint64_t read_off_pages = 0, num_ele = 0, range_bytes = 0, n_pages = 0, n_slots = 0;
+  uint64_t n_lines = 0, n_lines_local = 0;
   uint32_t row_layout = 0;  // source row stride (elements) for CPU-buffer fills / WB; 0 = unknown
 
   // sharding (page p is owned by rank p % world)
   uint32_t world = 1, rank = 0;
-  uint64_t n_pages_local = 0;
   bool shards_ready = true;           // false until peers are attached (world > 1)
   DevShard shards[GIDS_MAX_WORLD] = {};
   std::vector<void*> ipc_opened;      // peer shard bases opened through CUDA IPC

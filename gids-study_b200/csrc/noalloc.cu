@@ -24,7 +24,7 @@
 //  * the array is shared by all calls on a device: calls that overlap on the
 //    GPU (different streams, or an asynchronous store called again before the
 //    previous call finished) race on it;
-//  * a store whose page table does not fit (more than about 4M pages) is
+//  * a store whose page table does not fit (more than about 4M cache lines) is
 //    rejected with GIDS_E_RANGE before anything is launched;
 //  * no cudaMalloc, cudaFree or other allocating call is made.
 #include <cuda_runtime.h>
@@ -70,22 +70,22 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
   GIDS_CHECK(n == 0 || (out && idx), GIDS_E_INVAL, "null output or index pointer");
   // layout of the scratch: counters | clock | page table | slot tags | clock bits | slots
   const uint64_t off_stats = 0, off_clock = 256, off_state = 512;
-  const uint64_t off_tags = up(off_state + n_pages * 8, 256);
+  const uint64_t off_tags = up(off_state + n_lines * 8, 256);
   GIDS_CHECK(off_tags <= kNoallocScratchBytes, GIDS_E_RANGE,
-             "gids_read_feature_noalloc: the range has " + std::to_string(n_pages) +
-                 " pages; its page table does not fit the " + std::to_string(kNoallocScratchBytes >> 20) +
+             "gids_read_feature_noalloc: the range has " + std::to_string(n_lines) +
+                 " cache lines; its page table does not fit the " + std::to_string(kNoallocScratchBytes >> 20) +
                  " MiB no-allocation scratch (at most " + std::to_string((kNoallocScratchBytes - 512) / 8) +
-                 " pages)");
+                 " lines)");
   DeviceGuard g(device);
   check_async_error();
   char* base = scratch_address(device);
   const uint64_t room = kNoallocScratchBytes - off_tags;
   // slot tags (8 B) + clock bit (1 B) + page bytes per slot, pages 4 KB-aligned
-  uint64_t ns = room / (page_size + 9);
+  uint64_t ns = room / (line_size + 9);
   while (ns && up(off_tags + ns * 8, 256) + up(ns, 256) > kNoallocScratchBytes) ns--;
   uint64_t off_ref = up(off_tags + ns * 8, 256);
   uint64_t off_slots = up(off_ref + ns, 4096);
-  while (ns && off_slots + ns * (uint64_t)page_size > kNoallocScratchBytes) {
+  while (ns && off_slots + ns * (uint64_t)line_size > kNoallocScratchBytes) {
     ns--;
     off_ref = up(off_tags + ns * 8, 256);
     off_slots = up(off_ref + ns, 4096);
@@ -98,16 +98,16 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
                "dim exceeds the constant CPU buffer's row width (cpu_backing_buffer dim)");
     if (cpu_filled_stride != (uint32_t)cache_dim) fill_cpu_buffer((uint32_t)cache_dim);
   }
-  uint64_t gst = src_stride, b = page_size;
+  uint64_t gst = src_stride, b = line_size;
   while (b) {
     const uint64_t t = gst % b;
     gst = b;
     b = t;
   }
-  const uint64_t max_pages = (page_size - gst + row_bytes - 1) / page_size + 1;
+  const uint64_t max_pages = (line_size - gst + row_bytes - 1) / line_size + 1;
   uint32_t seg_shift = 0;
   while ((1ull << seg_shift) < max_pages) seg_shift++;
-  GIDS_CHECK(seg_shift <= 5, GIDS_E_UNSUPPORTED, "a row may span more than 32 pages; use larger pages");
+  GIDS_CHECK(seg_shift <= 5, GIDS_E_UNSUPPORTED, "a row may span more than 32 cache lines; use larger lines");
   int vec = 16;
   while (vec > 2 && (row_bytes % vec || src_stride % vec || (uint64_t)(uintptr_t)out % vec)) vec >>= 1;
   GIDS_CHECK(row_bytes % vec == 0 && src_stride % vec == 0, GIDS_E_INVAL, "rows must be 2-byte aligned");
@@ -117,7 +117,7 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
   // clear what must start at zero (INVALID pages, no counts, clock at 0) and
   // mark every slot empty; the slot bytes need no clearing
   GIDS_CUDA(cudaMemsetAsync(base + off_stats, 0, 512, st));
-  GIDS_CUDA(cudaMemsetAsync(base + off_state, 0, n_pages * 8, st));
+  GIDS_CUDA(cudaMemsetAsync(base + off_state, 0, n_lines * 8, st));
   if (ns) {
     GIDS_CUDA(cudaMemsetAsync(base + off_tags, 0xFF, ns * 8, st));
     GIDS_CUDA(cudaMemsetAsync(base + off_ref, 0, ns, st));
@@ -132,9 +132,9 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
   a.c.sh[0].slots = base + off_slots;
   a.c.sh[0].clock = (unsigned long long*)(base + off_clock);
   a.c.n_slots = ns;
-  a.c.n_pages = n_pages;
-  a.c.page_shift = page_shift;
-  a.c.page_size = page_size;
+  a.c.n_pages = n_lines;
+  a.c.page_shift = line_shift;
+  a.c.page_size = line_size;
   a.c.world = 1;
   a.c.rank = 0;
   a.b = dev_backing();

@@ -94,13 +94,13 @@ namespace {
 // peer's shard can be addressed from its base pointer alone.
 struct ShardLayout {
   uint64_t state, slot_page, slot_ref, wb, clock, slots, total;
-  ShardLayout(uint64_t n_pages_local, uint64_t n_slots, uint32_t page_size, bool with_wb) {
+  ShardLayout(uint64_t n_local, uint64_t n_slots, uint32_t page_size, bool with_wb) {
     auto up = [](uint64_t v, uint64_t a) { return (v + a - 1) / a * a; };
     state = 0;
-    slot_page = up(state + n_pages_local * 8, 256);
+    slot_page = up(state + n_local * 8, 256);
     slot_ref = up(slot_page + n_slots * 8, 256);
     wb = up(slot_ref + n_slots, 256);
-    clock = up(wb + (with_wb ? n_pages_local * 4 : 0), 256);
+    clock = up(wb + (with_wb ? n_local * 4 : 0), 256);
     slots = up(clock + 8, page_size > 4096 ? page_size : 4096);
     total = slots + n_slots * (uint64_t)page_size;
   }
@@ -139,7 +139,7 @@ void Store::open_peers(const void* handles, uint32_t n) {
   GIDS_CHECK(initialized, GIDS_E_STATE, "open_peers before init_controllers");
   GIDS_CHECK(n == world, GIDS_E_INVAL, "need one handle per rank");
   DeviceGuard g(device);
-  const ShardLayout L(n_pages_local, n_slots, page_size, world > 1);
+  const ShardLayout L(n_lines_local, n_slots, line_size, world > 1);
   const cudaIpcMemHandle_t* h = (const cudaIpcMemHandle_t*)handles;
   for (uint32_t r = 0; r < world; r++) {
     if (r == rank) continue;
@@ -157,8 +157,8 @@ void Store::share_in_process(Store* const* stores, uint32_t n) {
     Store* s = stores[i];
     GIDS_CHECK(s && s->initialized, GIDS_E_STATE, "every store must be initialised");
     GIDS_CHECK(s->world == n && s->rank == i, GIDS_E_INVAL, "store i must have world n and rank i");
-    GIDS_CHECK(s->n_pages == stores[0]->n_pages && s->n_slots == stores[0]->n_slots &&
-                   s->page_size == stores[0]->page_size,
+    GIDS_CHECK(s->n_lines == stores[0]->n_lines && s->n_slots == stores[0]->n_slots &&
+                   s->line_size == stores[0]->line_size,
                GIDS_E_INVAL, "stores differ in geometry");
   }
   for (uint32_t i = 0; i < n; i++)
@@ -196,7 +196,12 @@ void Store::init_controllers(Controllers* c, uint32_t ps, uint64_t read_off_page
   num_ele = ne;
   range_bytes = ne * elem_bytes;
   n_pages = (range_bytes + ps - 1) / ps;
-  n_slots = cache_mb * (1ull << 20) / ps;
+  line_size = line_request ? line_request : ps;
+  GIDS_CHECK(line_size >= 512 && (line_size & (line_size - 1)) == 0 && line_size <= ps, GIDS_E_INVAL,
+             "cache line must be a power of two in [512, page_size]");
+  line_shift = log2_exact(line_size);
+  n_lines = (range_bytes + line_size - 1) / line_size;
+  n_slots = cache_mb * (1ull << 20) / line_size;
   GIDS_CHECK(n_slots < (1ull << 32) - 1, GIDS_E_INVAL, "cache too large for 32-bit slot numbers");
 
   c->bind((uint32_t)num_ssd, ps, read_off_pages, n_pages);
@@ -205,9 +210,9 @@ void Store::init_controllers(Controllers* c, uint32_t ps, uint64_t read_off_page
 
   // this rank's shard: page table of the pages it owns (p % world == rank),
   // slots, clock and (when sharded) window-buffer pins, in one allocation
-  n_pages_local = (n_pages + world - 1) / world;
+  n_lines_local = (n_lines + world - 1) / world;
   const bool with_wb = world > 1;
-  const ShardLayout L(n_pages_local, n_slots, ps, with_wb);
+  const ShardLayout L(n_lines_local, n_slots, line_size, with_wb);
   shard_bytes = L.total;
   GIDS_CUDA(cudaMalloc(&d_shard, shard_bytes));
   const DevShard mine = L.at(d_shard, with_wb);
@@ -235,9 +240,9 @@ DevCache Store::dev_cache() const {
   for (uint32_t r = 0; r < world; r++) c.sh[r] = shards[r];
   if (world == 1) c.sh[0].wb = d_wb;  // allocated on first use
   c.n_slots = n_slots;
-  c.n_pages = n_pages;
-  c.page_shift = page_shift;
-  c.page_size = page_size;
+  c.n_pages = n_lines;
+  c.page_shift = line_shift;
+  c.page_size = line_size;
   c.world = world;
   c.rank = rank;
   return c;
@@ -249,6 +254,8 @@ DevBacking Store::dev_backing() const {
   b.n_ssd = ctrls->n_bound;
   b.page_start = ctrls->page_start;
   b.wrap_pages = ctrls->wrap_pages;
+  b.page_shift = page_shift;
+  b.lpp_shift = page_shift - line_shift;
   return b;
 }
 
@@ -289,6 +296,14 @@ void Store::fold_events(bool wait) {
   ev_pending.resize(keep);
 }
 
+void Store::set_cache_line(uint32_t bytes) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(!initialized, GIDS_E_STATE, "set_cache_line after init_controllers");
+  GIDS_CHECK(bytes == 0 || (bytes >= 512 && (bytes & (bytes - 1)) == 0), GIDS_E_INVAL,
+             "cache line must be 0 (the page) or a power of two >= 512");
+  line_request = bytes;
+}
+
 void Store::set_row_layout(uint32_t cache_dim) {
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(cache_dim > 0, GIDS_E_INVAL, "cache_dim must be > 0");
@@ -316,12 +331,12 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
   }
   if (!row_layout) row_layout = (uint32_t)cache_dim;
 
-  // lanes per row: pages one row can touch, rounded up to a power of two
-  const uint64_t gst = gcd64(src_stride, page_size);
-  const uint64_t max_pages = (page_size - gst + row_bytes - 1) / page_size + 1;
+  // lanes per row: cache lines one row can touch, rounded up to a power of two
+  const uint64_t gst = gcd64(src_stride, line_size);
+  const uint64_t max_pages = (line_size - gst + row_bytes - 1) / line_size + 1;
   uint32_t seg_shift = 0;
   while ((1ull << seg_shift) < max_pages) seg_shift++;
-  GIDS_CHECK(seg_shift <= 5, GIDS_E_UNSUPPORTED, "a row may span more than 32 pages; use larger pages");
+  GIDS_CHECK(seg_shift <= 5, GIDS_E_UNSUPPORTED, "a row may span more than 32 cache lines; use larger lines");
   const uint64_t rpc = 32ull >> seg_shift;
 
   // vector width: every address and length of the copy must be a multiple
@@ -409,8 +424,8 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   DeviceGuard g(device);
   if (!d_wb) {
-    GIDS_CUDA(cudaMalloc(&d_wb, n_pages * sizeof(unsigned int)));
-    GIDS_CUDA(cudaMemset(d_wb, 0, n_pages * sizeof(unsigned int)));
+    GIDS_CUDA(cudaMalloc(&d_wb, n_lines * sizeof(unsigned int)));
+    GIDS_CUDA(cudaMemset(d_wb, 0, n_lines * sizeof(unsigned int)));
   }
   // rows map to pages by bytes; without a known layout, one row per page
   // (the reference's assumption, gids_kernel.cu:251-252)
@@ -424,7 +439,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   w.stride = (uint64_t)se * elem_bytes;
   w.row_bytes = w.stride;
   w.n_rows = range_bytes >= w.row_bytes ? (range_bytes - w.row_bytes) / w.stride + 1 : 0;
-  w.page_shift = page_shift;
+  w.page_shift = line_shift;
   launch_wb_mark(w, st);
   last_stream = st;
   if (synchronous) GIDS_CUDA(cudaStreamSynchronize(st));
@@ -549,7 +564,7 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
   }
   // the cache and the CPU buffer may hold stale copies of the written pages
   // (a sharded cache drops this rank's shard; every rank has to flush)
-  GIDS_CUDA(cudaMemset(d_state, 0, n_pages_local * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_state, 0, n_lines_local * sizeof(unsigned long long)));
   if (n_slots) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
@@ -566,7 +581,7 @@ void Store::flush_cache() {
   GIDS_CHECK(initialized, GIDS_E_STATE, "flush_cache before init_controllers");
   DeviceGuard g(device);
   GIDS_CUDA(cudaDeviceSynchronize());
-  GIDS_CUDA(cudaMemset(d_state, 0, n_pages_local * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_state, 0, n_lines_local * sizeof(unsigned long long)));
   if (n_slots) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));

@@ -111,6 +111,13 @@ GIDS_API int gids_store_destroy(gids_store_t *s);
 /* 1 (default) = every gather synchronizes its stream before returning, like
  * the reference (gids_nvme.cu:335,348); 0 = stream-ordered, asynchronous. */
 GIDS_API int gids_store_set_synchronous(gids_store_t *s, int synchronous);
+/* Cache line (no reference counterpart; the reference caches whole pages):
+ * the unit of the GPU cache's page table, slots and fills, a power of two in
+ * [512, page_size] (0 = the page, the default). The stripe layout of the
+ * backing store keeps page_size. Smaller lines keep rows much smaller than a
+ * page from pulling whole pages over the host link. Call before
+ * gids_store_init_controllers. */
+GIDS_API int gids_store_set_cache_line(gids_store_t *s, uint32_t bytes);
 /* Source row stride (elements) used to fill the constant CPU buffer before
  * the first gather tells it (the reference assumes one row per page,
  * gids_nvme.cu:173,704). */
@@ -257,7 +264,7 @@ GIDS_API int gids_read_range_host(gids_store_t *s, void *dst, uint64_t nbytes, u
 GIDS_API int gids_fill_synthetic(gids_store_t *s, int kind, uint64_t seed, int threads);
 /* Geometry of the bound backing store: [0]=pages in the range, [1]=pages
  * physically held (wrap period), [2]=bytes per SSD, [3]=cache slots,
- * [4]=page size, [5]=number of SSDs. */
+ * [4]=page size, [5]=number of SSDs, [6]=cache line size. */
 GIDS_API int gids_store_geometry(gids_store_t *s, uint64_t *out, int count);
 
 #ifdef __cplusplus

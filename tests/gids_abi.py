@@ -67,6 +67,7 @@ def lib():
             "gids_fill_synthetic": (i32, [vp, i32, u64, i32]),
             "gids_store_geometry": (i32, [vp, P(u64), i32]),
             "gids_store_set_sharding": (i32, [vp, i32, i32]),
+            "gids_store_set_cache_line": (i32, [vp, u32]),
             "gids_store_ipc_handle": (i32, [vp, vp, ctypes.c_size_t]),
             "gids_store_open_peers": (i32, [vp, vp, i32]),
             "gids_store_share_shards": (i32, [P(vp), i32]),
@@ -103,7 +104,7 @@ class Store:
     """Thin owner of a gids_store_t + gids_ctrls_t pair."""
 
     def __init__(self, elem_bytes, page_size, num_ele, cache_mb, num_ssd=1, ssd_list=None, read_off_pages=0,
-                 capacity=0, pattern=None, device=0, synchronous=True, world=1, rank=0):
+                 capacity=0, pattern=None, device=0, synchronous=True, world=1, rank=0, cache_line=0):
         L = lib()
         self.c = ctypes.c_void_p()
         check(L.gids_ctrls_create(ctypes.byref(self.c)))
@@ -115,6 +116,8 @@ class Store:
         check(L.gids_store_create(ctypes.byref(self.s), elem_bytes, device))
         if world > 1:
             check(L.gids_store_set_sharding(self.s, world, rank))
+        if cache_line:
+            check(L.gids_store_set_cache_line(self.s, cache_line))
         check(L.gids_store_init_controllers(self.s, self.c, page_size, read_off_pages, cache_mb, num_ele, num_ssd))
         check(L.gids_store_set_synchronous(self.s, 1 if synchronous else 0))
         self.elem_bytes = elem_bytes
@@ -157,6 +160,7 @@ class Store:
         check(lib().gids_reset_stats(self.s))
 
     def geometry(self):
-        v = (ctypes.c_uint64 * 6)()
-        check(lib().gids_store_geometry(self.s, v, 6))
-        return dict(zip(["range_pages", "wrap_pages", "ssd_bytes", "cache_slots", "page_size", "num_ssd"], list(v)))
+        v = (ctypes.c_uint64 * 7)()
+        check(lib().gids_store_geometry(self.s, v, 7))
+        return dict(zip(["range_pages", "wrap_pages", "ssd_bytes", "cache_slots", "page_size", "num_ssd",
+                         "cache_line"], list(v)))

@@ -26,6 +26,7 @@ def bits_equal(a: torch.Tensor, b: np.ndarray) -> bool:
 
 
 def make_store(table: np.ndarray, page_size=4096, cache_mb=64, num_ssd=2, read_off=0, **kw) -> Store:
+    """Store holding `table` row-major at offset 0 (kw: capacity, pattern, cache_line, ...)."""
     s = Store(table.dtype.itemsize, page_size, table.size, cache_mb, num_ssd=num_ssd, read_off_pages=read_off, **kw)
     s.write_range(table.ctypes.data, table.nbytes, 0)
     return s
@@ -120,6 +121,54 @@ def test_geometries(page, ssds, off, cache_mb, rows, cdim, dim, dt):
     assert st["access"] == st["hit"] + st["miss"] + st["bypass"]
     assert st["rows"] == 3 * 2500 and st["bad_ids"] == 0 and st["wait_timeouts"] == 0
     s.close()
+
+
+LINE_GEOMETRIES = [
+    # page, cache line, ssds, cache_mb, rows, cache_dim, dim, dtype
+    (4096, 512, 4, 2, 20000, 128, 128, np.float32),    # config-5 rows: one 512 B line each
+    (4096, 512, 4, 2, 6000, 768, 768, np.float16),     # config-4 rows: three lines each
+    (4096, 1024, 3, 2, 6000, 768, 700, np.float16),    # rows straddle 1 KB lines
+    (8192, 2048, 2, 4, 4000, 1024, 1024, np.float32),  # 4 KB rows over 2 KB lines
+    (4096, 512, 2, 1, 5000, 33, 31, np.float32),       # 4-byte vectors
+]
+
+
+@pytest.mark.parametrize("page,line,ssds,cache_mb,rows,cdim,dim,dt", LINE_GEOMETRIES)
+def test_cache_lines_smaller_than_pages(page, line, ssds, cache_mb, rows, cdim, dim, dt):
+    kind = {np.float32: oracle.KIND_F32_UNIFORM, np.float16: oracle.KIND_F16_BYTESUM}[dt]
+    t = oracle.synth_table(kind, 17, rows, cdim)
+    s = make_store(t, page_size=page, cache_mb=cache_mb, num_ssd=ssds, cache_line=line)
+    g = s.geometry()
+    assert g["cache_line"] == line and g["cache_slots"] == cache_mb * (1 << 20) // line
+    rng = np.random.default_rng(line + rows)
+    for _ in range(3):
+        ids = rng.integers(0, rows, size=4000)
+        rc, out = gather(s, ids, dim, cdim, NP2T[np.dtype(dt)])
+        check(rc)
+        assert bits_equal(out, oracle.gather(t, ids, dim=dim))
+    st = s.stats()
+    assert st["access"] == st["hit"] + st["miss"] + st["bypass"] and st["wait_timeouts"] == 0
+    # a missed row moves only its lines: fills x line bytes stays within (rows' lines) x line bytes
+    assert st["read_io"] * line <= st["access"] * line
+    s.close()
+
+
+def test_cache_line_arguments():
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 1, 100, 256)
+    L = gids_abi.lib()
+    for bad in (256, 3000, 8192):  # below 512, not a power of two, above the page
+        c = ctypes.c_void_p()
+        check(L.gids_ctrls_create(ctypes.byref(c)))
+        lst = (ctypes.c_int32 * 1)(0)
+        check(L.gids_ctrls_init(c, 1, 1024, 128, lst))
+        st = ctypes.c_void_p()
+        check(L.gids_store_create(ctypes.byref(st), 4, 0))
+        rc = L.gids_store_set_cache_line(st, bad)
+        if rc == gids_abi.GIDS_OK:
+            rc = L.gids_store_init_controllers(st, c, 4096, 0, 1, t.size, 1)
+        assert rc == gids_abi.GIDS_E_INVAL, bad
+        check(L.gids_store_destroy(st))
+        check(L.gids_ctrls_destroy(c))
 
 
 def test_small_cache_evicts_and_stays_exact():

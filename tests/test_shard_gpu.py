@@ -30,7 +30,7 @@ def bits_equal(a: torch.Tensor, b: np.ndarray) -> bool:
 class Shared:
     """Controllers + `world` stores on one device, shards shared in-process."""
 
-    def __init__(self, table, world, page=4096, cache_mb=1, num_ssd=2, device=0):
+    def __init__(self, table, world, page=4096, cache_mb=1, num_ssd=2, device=0, line=0):
         L = gids_abi.lib()
         self.c = ctypes.c_void_p()
         check(L.gids_ctrls_create(ctypes.byref(self.c)))
@@ -43,6 +43,8 @@ class Shared:
             s = ctypes.c_void_p()
             check(L.gids_store_create(ctypes.byref(s), table.dtype.itemsize, device))
             check(L.gids_store_set_sharding(s, world, r))
+            if line:
+                check(L.gids_store_set_cache_line(s, line))
             check(L.gids_store_init_controllers(s, self.c, page, 0, cache_mb, table.size, num_ssd))
             self.s.append(s)
         arr = (ctypes.c_void_p * world)(*self.s)
@@ -130,6 +132,20 @@ def test_in_process_shards_churn(world):
         tot = [sh.stats(r) for r in range(world)]
         assert sum(s["evictions"] for s in tot) > 0
         assert all(s["access"] == s["hit"] + s["miss"] + s["bypass"] for s in tot)
+    finally:
+        sh.close()
+
+
+def test_in_process_shards_with_small_lines():
+    rows, cdim = 30000, 128  # 512-byte rows, 512-byte cache lines, 4 KB stripe pages
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 24, rows, cdim)
+    sh = Shared(t, 2, cache_mb=1, line=512)
+    rng = np.random.default_rng(24)
+    try:
+        for k in range(4):
+            ids = rng.integers(0, rows, size=9000)
+            out = sh.gather(k % 2, ids, cdim, cdim)
+            assert bits_equal(out, oracle.gather(t, ids))
     finally:
         sh.close()
 

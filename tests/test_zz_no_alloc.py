@@ -73,6 +73,22 @@ def test_noalloc_straddling_rows_and_cpu_buffer():
         s.close()
 
 
+def test_noalloc_with_small_cache_lines():
+    rows, cdim = 30000, 128  # 512-byte rows in 512-byte lines of 4 KB pages
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 43, rows, cdim)
+    s = Store(4, 4096, t.size, 1, num_ssd=2, cache_line=512)
+    s.write_range(t.ctypes.data, t.nbytes, 0)
+    rng = np.random.default_rng(43)
+    try:
+        for call in range(2):
+            ids = rng.integers(0, rows, size=7000)
+            ref, got = _pair(s, ids, cdim, cdim, torch.float32)
+            assert got.tobytes() == ref.tobytes(), f"call {call}"
+            assert got.tobytes() == oracle.gather(t, ids).tobytes()
+    finally:
+        s.close()
+
+
 def test_noalloc_rejects_a_page_table_beyond_the_scratch():
     page, cdim = 4096, 1024
     pages = 8 << 20  # 8M pages: a 64 MiB page table, the scratch holds 32 MiB
