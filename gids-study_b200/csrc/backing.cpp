@@ -13,9 +13,11 @@
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
+#include <sys/syscall.h>
 #include <unistd.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <thread>
 
@@ -51,6 +53,37 @@ bool cuda_device_present() {
   return cudaGetDeviceCount(&n) == cudaSuccess && n > 0;
 }
 
+// Spread a mapping's pages over all online NUMA nodes (MPOL_INTERLEAVE via
+// the raw mbind syscall; best effort, nothing to do on a single-node host),
+// so that GPUs attached to different sockets share the memory bandwidth of
+// all sockets when they read the backing store.
+void interleave_numa(void* p, uint64_t bytes) {
+  FILE* f = fopen("/sys/devices/system/node/online", "r");
+  if (!f) return;
+  char buf[256] = {0};
+  const size_t n = fread(buf, 1, sizeof(buf) - 1, f);
+  fclose(f);
+  if (!n) return;
+  unsigned long mask[16] = {0};
+  int count = 0;
+  for (char* tok = strtok(buf, ",\n"); tok; tok = strtok(nullptr, ",\n")) {
+    int a = -1, b = -1;
+    if (sscanf(tok, "%d-%d", &a, &b) == 2) {
+    } else if (sscanf(tok, "%d", &a) == 1) {
+      b = a;
+    } else {
+      continue;
+    }
+    for (int i = a; i <= b && i >= 0 && i < 1024; i++) {
+      mask[i / 64] |= 1ul << (i % 64);
+      count++;
+    }
+  }
+  if (count < 2) return;
+  constexpr int kMpolInterleave = 3;
+  syscall(SYS_mbind, p, bytes, kMpolInterleave, mask, 1024ul, 0u);
+}
+
 // Touch every page so that the region is backed (and huge pages are formed)
 // before it is pinned. Anonymous memory is zeroed; file memory is only read.
 void prefault(char* p, uint64_t bytes, bool write_zero, int threads) {
@@ -78,6 +111,7 @@ void PinnedHost::alloc(uint64_t nbytes, int threads) {
   void* p = mmap(nullptr, nbytes, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS | MAP_NORESERVE, -1, 0);
   GIDS_CHECK(p != MAP_FAILED, GIDS_E_NOMEM, "mmap of " + std::to_string(nbytes) + " bytes failed");
   madvise(p, nbytes, MADV_HUGEPAGE);
+  interleave_numa(p, nbytes);
   host = (char*)p;
   bytes = nbytes;
   prefault(host, bytes, true, threads);
@@ -172,12 +206,14 @@ uint64_t Controllers::bind(uint32_t n, uint32_t ps, uint64_t start, uint64_t pag
       GIDS_CHECK(p != MAP_FAILED, GIDS_E_IO, "cannot map emulated SSD " + path);
       s.host = (char*)p;
       madvise(p, bytes, MADV_HUGEPAGE);
+      interleave_numa(p, bytes);
       prefault(s.host, bytes, false, threads);
     } else {
       void* p = mmap(nullptr, bytes, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS | MAP_NORESERVE, -1, 0);
       GIDS_CHECK(p != MAP_FAILED, GIDS_E_NOMEM, "cannot allocate emulated SSD of " + std::to_string(bytes) + " bytes");
       s.host = (char*)p;
       madvise(p, bytes, MADV_HUGEPAGE);
+      interleave_numa(p, bytes);
       prefault(s.host, bytes, true, threads);
     }
   }
