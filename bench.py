@@ -70,6 +70,11 @@ CONFIGS = {
     "c5": dict(BASE, nodes=500_000_000, mean_deg=10, alpha=1.1, dim=128, dtype="float32", page=4096, ssds=8,
                cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None, line=512),
 }
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per gathered row of gather_kernel, from one
+# ncu --set full capture of a small case of the same config with the same hit/fill mix
+# (config 2: 4M nodes, 2 GB cache, batch 512 -> 3.182 GB over 366,578 rows); a full launch's
+# traffic is this times its rows. Configs without such a capture report null.
+TRAFFIC_PER_ROW = {"c2": 3.182e9 / 366578}
 KIND = {"float32": 1, "float16": 2}
 TDTYPE = {"float32": torch.float32, "float16": torch.float16}
 ESIZE = {"float32": 4, "float16": 2}
@@ -223,13 +228,25 @@ def make_batches(cfg, n_batches, rank, device, with_pins=False):
     return out, time.time() - t0
 
 
-def host_link_peak_gbs(device) -> float:
-    """Pinned host -> device copy bandwidth (GB/s), best of 3 x 1 GiB."""
+# untimed cache warm-up, in cache-sizes of line references
+CACHE_WARMUP_CACHES = 12
+
+# cache replacement policies: (admission on the second miss, clock counter ceiling)
+POLICIES = {"admit2": (True, 3), "clock": (False, 1), "admit2_sc": (True, 1), "clock3": (False, 3)}
+
+
+def host_link_peak_gbs(device, dist=None) -> float:
+    """Pinned host -> device copy bandwidth (GB/s), best of 4 x 1 GiB. With
+    several ranks, all ranks copy at the same time (a barrier before each
+    copy), which is the link bandwidth one GPU gets while the others also read
+    host memory."""
     n = 1 << 30
     h = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     d = torch.empty(n, dtype=torch.uint8, device=device)
     best = 0.0
     for _ in range(4):
+        if dist is not None:
+            dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         d.copy_(h, non_blocking=True)
@@ -342,7 +359,8 @@ def run_ours(args, cfg, dist: Dist):
                   dtype=TDTYPE[dt], ssd_capacity=per_ssd if phys < range_bytes else 0, ssd_path=pattern,
                   synchronous=False, shard_cache=shared and not args.no_shard, window_buffer=cfg["wb"] > 0,
                   wb_size=max(1, cfg["wb"]), cache_line=cfg["line"] or None,
-                  heterograph=cfg["hetero"] is not None, heterograph_map=hmap)
+                  heterograph=cfg["hetero"] is not None, heterograph_map=hmap,
+                  cache_admission=POLICIES[args.policy][0], cache_ref_max=POLICIES[args.policy][1])
     t_store = time.time() - t0
     if not shared:
         t0 = time.time()
@@ -376,14 +394,39 @@ def run_ours(args, cfg, dist: Dist):
     # generators: a batch list (and the features appended to it) lives only until the step ends
     dev_it = ([b] for b in batches[:args.warmup + args.steps + wb])
 
-    # warm-up (fills the cache)
+    # cache warm-up: minibatches from other sampler seeds, untimed, so that the
+    # timed steps see the page cache of a job that has been training for a while
+    # (admission fills the cache with lines that recur, which takes several
+    # cache-sizes of line references); then the W warm-up steps
+    line = geo.get("cache_line", page)
+    refs_per_batch = float(np.mean(sizes)) * -(-row_bytes // line)
+    n_cw = args.cache_warmup
+    if n_cw < 0:
+        n_cw = int(min(60, math.ceil(CACHE_WARMUP_CACHES * geo["cache_slots"] / max(1.0, refs_per_batch))))
+    t0 = time.time()
+    wbf = g.window_buffering_flag
+    g.window_buffering_flag = False  # the warm-up leaves no window pins behind
+    done, k = 0, 0
+    while done < n_cw:
+        m = min(8, n_cw - done)
+        k += 1
+        wbatches, _ = make_batches(cfg, m, dist.rank + 7919 * k, device)
+        wit = ([b] for b in wbatches)
+        for _ in range(m):
+            g.fetch_feature(dim, wit, device)
+        done += m
+        del wbatches, wit
+    torch.cuda.synchronize()
+    g.window_buffering_flag = wbf
+    t_cw = time.time() - t0
+    log(f"[rank {dist.rank}] cache warm-up: {n_cw} minibatches in {t_cw:.1f}s")
     for i in range(args.warmup):
         g.fetch_feature(dim, dev_it, device)
     torch.cuda.synchronize()
     bam.reset_stats()
 
     hbm_peak, hbm_src = measured_hbm_peak()
-    host_peak = host_link_peak_gbs(device) if dist.rank == 0 or True else 0.0
+    host_peak = host_link_peak_gbs(device, dist)
 
     # ---- timed region 1: node ids resident in HBM
     clocks = ClockSampler(dist.local)
@@ -463,9 +506,11 @@ def run_ours(args, cfg, dist: Dist):
     acc = max(1, st["access"])
     roofline = {
         "bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": unit_peak,
-        "frac": round(t_star / t_launch, 4), "traffic": None,
+        "frac": round(t_star / t_launch, 4),
+        "traffic": (int(TRAFFIC_PER_ROW[args.config] * rows_l) if args.config in TRAFFIC_PER_ROW and not args.nodes
+                    else None),
         "peak_source": (hbm_src + " (of measured)") if bound == "hbm" else
-        "pinned host->device copy measured live in this run (of measured)",
+        "pinned host->device copy measured live in this run, all ranks copying at once (of measured)",
         "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss)/BW_host); frac = T*/T_launch",
         "t_launch_ms": round(t_launch * 1e3, 3), "t_star_ms": round(t_star * 1e3, 3),
         "hbm": {"alg_bytes_per_launch": int(alg_hbm), "achieved_gbs": round(alg_hbm / t_launch / 1e9, 1),
@@ -498,7 +543,9 @@ def run_ours(args, cfg, dist: Dist):
                           if min(sizes) * row_bytes > 126e6 else "steps smaller than L2: not a timing run"),
                    "input_nodes_per_step": round(rows_val / max(1, len(dev_ids)), 1),
                    "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
-                   "window_buffer_depth": wb},
+                   "window_buffer_depth": wb,
+                   "cache_policy": args.policy,
+                   "cache_warmup_minibatches": n_cw},
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "api": "GIDS.fetch_feature",
                 "h2d_bytes_per_step": int(np.mean([nrows(b) * 8 for b in e2e_batches])),
@@ -507,7 +554,8 @@ def run_ours(args, cfg, dist: Dist):
                 "mix": {"hit": round(st_e2e["hit"] / max(1, st_e2e["access"]), 4)}},
         "gpu_launches": int(launches) + (len(dev_ids) if wb else 0),
         "clocks": clk,
-        "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1)},
+        "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1),
+                    "cache_warmup": round(t_cw, 1)},
     }
     torch.cuda.synchronize()
     g.close()
@@ -557,6 +605,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-shard", action="store_true", help="N>1: independent caches instead of one sharded cache")
     ap.add_argument("--cache-line", type=int, default=-1, help="cache line bytes (0 = the page; -1 = the config's)")
+    ap.add_argument("--cache-warmup", type=int, default=-1,
+                    help="untimed minibatches (other sampler seeds) gathered before the warm-up steps; -1: "
+                         "enough for about 12 cache-sizes of line references, at most 60")
+    ap.add_argument("--policy", default="admit2", choices=sorted(POLICIES),
+                    help="cache replacement: admit2 = insert on the second miss + 2-bit clock; clock = insert "
+                         "every miss + second-chance clock (the reference's insertion rule)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3")

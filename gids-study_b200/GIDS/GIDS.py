@@ -72,13 +72,18 @@ class GIDS:
     with the same geometry, and call ``close()`` collectively. ``cache_line``
     (bytes, a power of two in [512, page_size]; default the page) sets the
     unit the GPU cache holds and fetches, so that rows much smaller than a
-    page do not pull whole pages over the host link.
+    page do not pull whole pages over the host link. ``cache_admission``
+    (default True) inserts a line on its second miss within a window of twice
+    the cache's slots, so lines touched once do not evict lines touched often;
+    ``cache_ref_max`` (default 3) is the clock counter ceiling (1 = the
+    second-chance clock). Neither changes what is gathered.
     """
 
     def __init__(self, page_size=4096, off=0, cache_dim=1024, num_ele=300 * 1000 * 1000 * 1024, num_ssd=1,
                  ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
                  long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
-                 ssd_path=None, synchronous=False, shard_cache=False, process_group=None, cache_line=None):
+                 ssd_path=None, synchronous=False, shard_cache=False, process_group=None, cache_line=None,
+                 cache_admission=True, cache_ref_max=3):
         if dtype is None:
             dtype = torch.int64 if long_type else torch.float32
         if dtype not in _STORE_CLASSES:
@@ -138,6 +143,7 @@ class GIDS:
         if self.world > 1:
             self._attach_peer_shards()
         self.BAM_FS.set_row_layout(cache_dim)
+        self.BAM_FS.set_cache_policy(bool(cache_admission), int(cache_ref_max))
         self.BAM_FS.set_synchronous(bool(synchronous))
         self.synchronous = bool(synchronous)
 

@@ -196,6 +196,28 @@ int gids_store_set_cache_line(gids_store_t* s, uint32_t bytes) {
   });
 }
 
+int gids_store_set_wait_limit(gids_store_t* s, uint32_t polls) {
+  return guarded([&] {
+    NEED(s);
+    GIDS_CHECK(polls >= 1, GIDS_E_INVAL, "at least one poll");
+    s->s.wait_limit = polls;
+  });
+}
+
+int gids_store_set_cache_policy(gids_store_t* s, int admission, uint32_t ref_max) {
+  return guarded([&] {
+    NEED(s);
+    s->s.set_policy(admission != 0, ref_max);
+  });
+}
+
+int gids_store_debug_mark_busy(gids_store_t* s, uint64_t line) {
+  return guarded([&] {
+    NEED(s);
+    s->s.debug_mark_busy(line);
+  });
+}
+
 int gids_store_set_row_layout(gids_store_t* s, uint32_t cache_dim) {
   return guarded([&] {
     NEED(s);

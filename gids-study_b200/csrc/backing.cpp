@@ -186,6 +186,7 @@ uint64_t Controllers::bind(uint32_t n, uint32_t ps, uint64_t start, uint64_t pag
   const uint64_t bytes = cap_pages * (uint64_t)ps;
   ssd.assign(n, SsdRegion{});
   const int threads = hw_threads();
+  try {
   for (uint32_t i = 0; i < n; i++) {
     SsdRegion& s = ssd[i];
     s.bytes = bytes;
@@ -216,6 +217,14 @@ uint64_t Controllers::bind(uint32_t n, uint32_t ps, uint64_t start, uint64_t pag
       interleave_numa(p, bytes);
       prefault(s.host, bytes, true, threads);
     }
+  }
+  } catch (...) {  // release what was mapped before the failure
+    for (auto& r : ssd) {
+      if (r.host) munmap(r.host, r.bytes);
+      if (r.fd >= 0) close(r.fd);
+    }
+    ssd.clear();
+    throw;
   }
   bound = true;
   return wrap_pages;

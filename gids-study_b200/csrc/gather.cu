@@ -59,6 +59,15 @@ __device__ __forceinline__ unsigned long long atom_or_acquire(unsigned long long
   return r;
 }
 template <bool SYS>
+__device__ __forceinline__ unsigned long long atom_or_relaxed(unsigned long long* p, unsigned long long v) {
+  unsigned long long r;
+  if (SYS)
+    asm volatile("atom.relaxed.sys.global.or.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  else
+    asm volatile("atom.relaxed.gpu.global.or.b64 %0, [%1], %2;" : "=l"(r) : "l"(p), "l"(v) : "memory");
+  return r;
+}
+template <bool SYS>
 __device__ __forceinline__ void atom_and_relaxed(unsigned long long* p, unsigned long long v) {
   unsigned long long r;
   if (SYS)
@@ -283,12 +292,18 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
   __shared__ SegDesc seg_sh[WARPS][32];
   __shared__ unsigned long long cnt_sh[WARPS][K_N];  // warp-private counters
   __shared__ unsigned char fill_lane[WARPS][8];      // owner lanes of one fill batch
+  __shared__ unsigned char gate_sh[GIDS_MAX_WORLD];   // shard filters first misses (full, admission on)
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   SegDesc* sd = seg_sh[wib];
   unsigned long long* acc = cnt_sh[wib];
   if (lane < K_N) acc[lane] = 0;
-  __syncwarp();
+  // a shard admits every miss until its clock hand has gone round once (the
+  // cache is full); read once per block, a stale "not full" only admits more
+  if (threadIdx.x < GIDS_MAX_WORLD)
+    gate_sh[threadIdx.x] = threadIdx.x < a.c.world && a.c.sh[threadIdx.x].seen &&
+                           ld_relaxed<SYS>(a.c.sh[threadIdx.x].clock) >= a.c.n_slots;
+  __syncthreads();
   const uint32_t seg_shift = a.seg_shift;
   const uint32_t seg_mask = (1u << seg_shift) - 1u;
   const uint32_t rpc = 32u >> seg_shift;
@@ -366,14 +381,27 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         } else if (old & ST_BUSY) {
           cls = CLS_WAIT;
         } else {
-          const unsigned long long prev = atom_or_acquire<SYS>(stw, ST_BUSY);
-          if (prev & ST_VALID) {
-            cls = CLS_HIT;
-            slot = prev >> ST_SLOT_SHIFT;
-          } else if (prev & ST_BUSY) {
-            cls = CLS_WAIT;
+          // a miss: without an admission bit from an earlier miss in this
+          // window, read the line straight from the backing store
+          // (a line that window buffering has pinned for later batches is
+          // admitted at once)
+          bool admit = true;
+          if (gate_sh[owner] && !(S.wb && ld_relaxed_u32<SYS>(S.wb + lp) > cnt)) {
+            const unsigned long long bit = 1ull << (lp & 63);
+            admit = (atom_or_relaxed<SYS>(S.seen + (lp >> 6), bit) & bit) != 0;
+          }
+          if (!admit) {
+            cls = CLS_BYPASS;
           } else {
-            cls = CLS_OWN;
+            const unsigned long long prev = atom_or_acquire<SYS>(stw, ST_BUSY);
+            if (prev & ST_VALID) {
+              cls = CLS_HIT;
+              slot = prev >> ST_SLOT_SHIFT;
+            } else if (prev & ST_BUSY) {
+              cls = CLS_WAIT;
+            } else {
+              cls = CLS_OWN;
+            }
           }
         }
       }
@@ -404,8 +432,8 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
           unsigned long long expect = 0;
           if (q == SLOT_EMPTY) {
             cand = true;
-          } else if (V.slot_ref[s]) {
-            V.slot_ref[s] = 0;  // second chance
+          } else if (const unsigned char rr = V.slot_ref[s]) {
+            V.slot_ref[s] = rr - 1;  // the clock hand spends one chance
           } else {
             const unsigned long long st = ld_relaxed<SYS>(V.state + q);
             if (st == (((unsigned long long)s << ST_SLOT_SHIFT) | ST_VALID) &&
@@ -601,7 +629,10 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     // ---- release, clock reference bit, window-buffer consumption
     if (took_ref) {
       red_add_release<SYS>(stw, (unsigned long long)(-(long long)cnt));
-      if (gcls != CLS_BYPASS) S.slot_ref[gslot] = 1;
+      if (gcls != CLS_BYPASS) {  // one more chance, up to the ceiling
+        const unsigned char rr = S.slot_ref[gslot];
+        if (rr < a.c.ref_max) S.slot_ref[gslot] = rr + 1;
+      }
       if (S.wb) wb_consume<SYS>(S.wb + lp, cnt);
     }
 

@@ -76,10 +76,11 @@ enum : int { CLS_NONE = 0, CLS_HIT = 1, CLS_OWN = 2, CLS_WAIT = 3, CLS_WAITED = 
 struct DevShard {
   unsigned long long* state;      // [n_pages_local] page table
   unsigned long long* slot_page;  // [n_slots] local page index held by each slot (SLOT_EMPTY if none)
-  unsigned char* slot_ref;        // [n_slots] clock reference bit
+  unsigned char* slot_ref;        // [n_slots] clock counter (chances left before eviction)
   unsigned int* wb;               // [n_pages_local] window-buffer pins, or nullptr
   char* slots;                    // [n_slots * page_size] resident pages
   unsigned long long* clock;      // clock hand
+  unsigned long long* seen;       // [n_pages_local / 64 + 1] admission bits, or nullptr (admit every miss)
 };
 
 // The cache works in lines: a line is the unit of the page table, of a slot
@@ -94,6 +95,7 @@ struct DevCache {
   uint32_t page_size;   // line size in bytes
   uint32_t world;  // ranks sharing the cache (1 = unsharded)
   uint32_t rank;
+  uint32_t ref_max;  // clock counter ceiling: 1 = second chance, >1 = frequency clock
 };
 
 struct DevBacking {
@@ -227,6 +229,14 @@ class Store {
   void set_cpu_buffer(const int64_t* host_idx, int64_t num);
   void set_row_layout(uint32_t cache_dim);
   void set_cache_line(uint32_t bytes);
+  void debug_mark_busy(uint64_t line);
+  uint32_t wait_limit = 1u << 16;  // polls of a BUSY line before giving up and bypassing
+  // replacement policy: admission (a line is inserted on its second miss
+  // within a window of 2 x n_slots line references) and clock counter ceiling
+  bool admission = true;
+  uint32_t ref_max = 3;
+  uint64_t refs_since_seen_reset = 0;
+  void set_policy(bool admit, uint32_t ref_ceiling);
   // gather with the page cache in the library's static no-allocation scratch (noalloc.cu)
   void read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
                     cudaStream_t st);

@@ -137,6 +137,7 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
   a.c.page_size = line_size;
   a.c.world = 1;
   a.c.rank = 0;
+  a.c.ref_max = 1;  // per-call cache: second-chance clock, every miss admitted (seen = nullptr)
   a.b = dev_backing();
   a.cpu = dev_cpu();
   a.stats = (unsigned long long*)(base + off_stats);
@@ -145,7 +146,7 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
   a.n_rows = range_bytes >= row_bytes ? (range_bytes - row_bytes) / src_stride + 1 : 0;
   a.row_bytes = (uint32_t)row_bytes;
   a.seg_shift = seg_shift;
-  a.spin_limit = 1u << 16;
+  a.spin_limit = wait_limit;
   a.sweep_limit = 64;
   a.k = 1;
   a.t[0].idx = idx;

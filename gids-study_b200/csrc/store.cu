@@ -3,6 +3,7 @@
 // reference's BAM_Feature_Store<T> (gids_module/include/bam_nvme.h:230-613,
 // gids_module/gids_nvme.cu:123-806).
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <cinttypes>
@@ -15,6 +16,12 @@
 namespace gids {
 
 namespace {
+// NVTX range for the duration of a host call (visible in Nsight traces)
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
+
 uint32_t log2_exact(uint64_t v) {
   uint32_t s = 0;
   while ((1ull << s) < v) s++;
@@ -93,7 +100,7 @@ namespace {
 // Byte layout of one shard allocation; identical on every rank so that a
 // peer's shard can be addressed from its base pointer alone.
 struct ShardLayout {
-  uint64_t state, slot_page, slot_ref, wb, clock, slots, total;
+  uint64_t state, slot_page, slot_ref, wb, clock, seen, seen_bytes, slots, total;
   ShardLayout(uint64_t n_local, uint64_t n_slots, uint32_t page_size, bool with_wb) {
     auto up = [](uint64_t v, uint64_t a) { return (v + a - 1) / a * a; };
     state = 0;
@@ -101,7 +108,9 @@ struct ShardLayout {
     slot_ref = up(slot_page + n_slots * 8, 256);
     wb = up(slot_ref + n_slots, 256);
     clock = up(wb + (with_wb ? n_local * 4 : 0), 256);
-    slots = up(clock + 8, page_size > 4096 ? page_size : 4096);
+    seen = up(clock + 8, 256);
+    seen_bytes = (n_local / 64 + 1) * 8;
+    slots = up(seen + seen_bytes, page_size > 4096 ? page_size : 4096);
     total = slots + n_slots * (uint64_t)page_size;
   }
   DevShard at(char* base, bool with_wb) const {
@@ -111,6 +120,7 @@ struct ShardLayout {
     d.slot_ref = (unsigned char*)(base + slot_ref);
     d.wb = with_wb ? (unsigned int*)(base + wb) : nullptr;
     d.clock = (unsigned long long*)(base + clock);
+    d.seen = (unsigned long long*)(base + seen);
     d.slots = base + slots;
     return d;
   }
@@ -245,6 +255,9 @@ DevCache Store::dev_cache() const {
   c.page_size = line_size;
   c.world = world;
   c.rank = rank;
+  c.ref_max = ref_max;
+  if (!admission)
+    for (uint32_t r = 0; r < world; r++) c.sh[r].seen = nullptr;
   return c;
 }
 
@@ -296,6 +309,24 @@ void Store::fold_events(bool wait) {
   ev_pending.resize(keep);
 }
 
+void Store::debug_mark_busy(uint64_t line) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "debug_mark_busy before init_controllers");
+  GIDS_CHECK(line < n_lines, GIDS_E_RANGE, "line outside the range");
+  GIDS_CHECK(world == 1 || line % world == rank, GIDS_E_INVAL, "the line is owned by another rank's shard");
+  DeviceGuard g(device);
+  GIDS_CUDA(cudaDeviceSynchronize());
+  const unsigned long long busy = ST_BUSY;  // BUSY, no references, not VALID, no slot
+  GIDS_CUDA(cudaMemcpy(d_state + (world == 1 ? line : line / world), &busy, sizeof(busy), cudaMemcpyHostToDevice));
+}
+
+void Store::set_policy(bool admit, uint32_t ref_ceiling) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(ref_ceiling >= 1 && ref_ceiling <= 255, GIDS_E_INVAL, "clock counter ceiling must be in [1, 255]");
+  admission = admit;
+  ref_max = ref_ceiling;
+}
+
 void Store::set_cache_line(uint32_t bytes) {
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(!initialized, GIDS_E_STATE, "set_cache_line after init_controllers");
@@ -314,6 +345,7 @@ void Store::set_row_layout(uint32_t cache_dim) {
 void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
                        int cache_dim, const uint64_t* key_offs, cudaStream_t st) {
   std::lock_guard<std::mutex> lk(mu);
+  NvtxRange nv("gids.read_feature");
   GIDS_CHECK(initialized, GIDS_E_STATE, "read_feature before init_controllers");
   GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   GIDS_CHECK(k >= 0, GIDS_E_INVAL, "k must be >= 0");
@@ -363,9 +395,20 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
   a.n_rows = range_bytes >= row_bytes ? (range_bytes - row_bytes) / src_stride + 1 : 0;
   a.row_bytes = (uint32_t)row_bytes;
   a.seg_shift = seg_shift;
-  a.spin_limit = 1u << 16;
+  a.spin_limit = wait_limit;
   a.sweep_limit = 64;
   uint64_t rows_total = 0;
+  if (admission && n_slots) {
+    // age the admission bits: clear this shard's after 2 x n_slots line references
+    uint64_t refs = 0;
+    for (int i = 0; i < k; i++) refs += ns[i] * max_pages;
+    refs_since_seen_reset += refs;
+    if (refs_since_seen_reset > 2 * n_slots) {
+      const ShardLayout Ls(n_lines_local, n_slots, line_size, world > 1);
+      GIDS_CUDA(cudaMemsetAsync(d_shard + Ls.seen, 0, Ls.seen_bytes, st));
+      refs_since_seen_reset = refs;
+    }
+  }
   for (int base = 0; base < k || (k == 0 && base == 0); base += GIDS_MAX_TUPLES) {
     const int kk = std::min(GIDS_MAX_TUPLES, k - base);
     uint64_t chunks = 0;
@@ -417,6 +460,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
 
 void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st) {
   std::lock_guard<std::mutex> lk(mu);
+  NvtxRange nv("gids.window_buffering");
   GIDS_CHECK(initialized, GIDS_E_STATE, "set_window_buffering before init_controllers");
   GIDS_CHECK(n >= 0, GIDS_E_INVAL, "n must be >= 0");
   if (n == 0) return;
@@ -586,6 +630,12 @@ void Store::flush_cache() {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
   }
+  // and forget which lines missed once; the clock restarts, so the empty
+  // cache admits every miss again
+  const ShardLayout L(n_lines_local, n_slots, line_size, world > 1);
+  GIDS_CUDA(cudaMemset(d_shard + L.seen, 0, L.seen_bytes));
+  GIDS_CUDA(cudaMemset(d_shard + L.clock, 0, 8));
+  refs_since_seen_reset = 0;
   GIDS_CUDA(cudaDeviceSynchronize());
 }
 

@@ -118,6 +118,26 @@ GIDS_API int gids_store_set_synchronous(gids_store_t *s, int synchronous);
  * page from pulling whole pages over the host link. Call before
  * gids_store_init_controllers. */
 GIDS_API int gids_store_set_cache_line(gids_store_t *s, uint32_t bytes);
+/* Replacement policy (no reference counterpart; the reference inserts every
+ * missed page and evicts with a clock that has no reference bits,
+ * page_cache_backup.h:2107-2256). admission = 1 (default): a line is inserted
+ * on its second miss within a window of 2 x (cache slots) line references;
+ * its first miss reads the backing store directly, so lines touched once do
+ * not evict lines touched often. ref_max (default 3): a hit adds a chance up
+ * to ref_max and the clock hand spends one per pass (1 = second chance).
+ * Results do not depend on the policy; only hit ratios do. */
+GIDS_API int gids_store_set_cache_policy(gids_store_t *s, int admission, uint32_t ref_max);
+/* Bounded waits (no reference counterpart; the reference spins forever,
+ * page_cache_backup.h:1389-1401): a gather polls a line that another warp or
+ * GPU is filling at most `polls` times (exponential back-off, 32 ns to 2 us),
+ * then reads the line from the backing store instead and counts a
+ * GIDS_STAT_WAIT_TIMEOUT. Default 65536 polls. */
+GIDS_API int gids_store_set_wait_limit(gids_store_t *s, uint32_t polls);
+/* Failure injection for tests: marks cache line `line` as being filled by a
+ * filler that never finishes (BUSY, no slot). The next gathers that need the
+ * line wait for it up to the wait limit, then bypass the cache. The store
+ * must be idle; the line must belong to the calling rank's shard. */
+GIDS_API int gids_store_debug_mark_busy(gids_store_t *s, uint64_t line);
 /* Source row stride (elements) used to fill the constant CPU buffer before
  * the first gather tells it (the reference assumes one row per page,
  * gids_nvme.cu:173,704). */

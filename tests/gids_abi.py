@@ -13,6 +13,7 @@ GIDS_E_INVAL = -1
 GIDS_E_CUDA = -2
 GIDS_E_STATE = -4
 GIDS_E_RANGE = -5
+GIDS_E_IO = -6
 GIDS_E_UNSUPPORTED = -7
 STAT_NAMES = ["access", "hit", "miss", "read_io", "bypass", "cpu_rows", "rows", "wait_timeouts", "bad_ids",
               "bytes_hit", "bytes_miss", "bytes_bypass", "bytes_cpu", "evictions", "launches", "bytes_peer"]
@@ -68,6 +69,9 @@ def lib():
             "gids_store_geometry": (i32, [vp, P(u64), i32]),
             "gids_store_set_sharding": (i32, [vp, i32, i32]),
             "gids_store_set_cache_line": (i32, [vp, u32]),
+            "gids_store_set_wait_limit": (i32, [vp, u32]),
+            "gids_store_set_cache_policy": (i32, [vp, i32, u32]),
+            "gids_store_debug_mark_busy": (i32, [vp, u64]),
             "gids_store_ipc_handle": (i32, [vp, vp, ctypes.c_size_t]),
             "gids_store_open_peers": (i32, [vp, vp, i32]),
             "gids_store_share_shards": (i32, [P(vp), i32]),
@@ -158,6 +162,9 @@ class Store:
 
     def reset_stats(self):
         check(lib().gids_reset_stats(self.s))
+
+    def set_policy(self, admission, ref_max):
+        check(lib().gids_store_set_cache_policy(self.s, 1 if admission else 0, ref_max))
 
     def geometry(self):
         v = (ctypes.c_uint64 * 7)()

@@ -126,3 +126,18 @@ def test_synthetic_fill_matches_oracle(built, kind):
     got = back.view(oracle.KIND_DTYPE[kind]).reshape(rows, cdim)
     exp = oracle.gather_synth(kind, 99, rows, cdim, cdim, np.arange(rows), wrap_elems=wrap * page // eb)
     assert got.tobytes() == exp.tobytes()
+
+
+def test_unopenable_emulated_ssd_is_an_io_error(built, tmp_path):
+    L = gids_abi.lib()
+    c = controllers(2, pattern=str(tmp_path / "no_such_dir" / "ssd{}"))
+    try:
+        assert L.gids_ctrls_bind(c, 2, 4096, 0, 1 << 20) == gids_abi.GIDS_E_IO
+        buf = ctypes.create_string_buffer(512)
+        L.gids_last_error(buf, 512)
+        assert b"cannot open emulated SSD" in buf.value
+        # unbound controllers refuse I/O
+        x = np.zeros(16, dtype=np.uint8)
+        assert L.gids_ctrls_write(c, x.ctypes.data, 16, 0) == gids_abi.GIDS_E_STATE
+    finally:
+        check(L.gids_ctrls_destroy(c))

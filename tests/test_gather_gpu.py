@@ -192,6 +192,7 @@ def test_hot_rows_hit_after_warmup():
     rows, cdim = 4000, 1024
     t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 5, rows, cdim)
     s = make_store(t, cache_mb=64)  # everything fits
+    s.set_policy(False, 1)  # insert on the first miss, as the reference does
     ids = np.arange(rows)
     check(gather(s, ids, cdim, cdim, torch.float32)[0])
     s.reset_stats()

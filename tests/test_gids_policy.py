@@ -114,7 +114,8 @@ def test_constructor_forwards_reference_arguments(fake):
     assert g.off == int(np.ceil(np.ceil((3 * 4096 * 2 + 1) / 4096) / 2))
     assert g.GIDS_controller.calls[0] == ("init", 2, 1024, 128, [5, 6])
     names = [c[0] for c in g.BAM_FS.calls]
-    assert names[:4] == ["set_device", "init_controllers", "set_row_layout", "set_synchronous"]
+    assert names[:5] == ["set_device", "init_controllers", "set_row_layout", "set_cache_policy", "set_synchronous"]
+    assert ("set_cache_policy", True, 3) in g.BAM_FS.calls
     assert g.BAM_FS.calls[1][2:] == (4096, g.off, 7, 1000 * 64, 2)
 
 

@@ -30,7 +30,7 @@ def bits_equal(a: torch.Tensor, b: np.ndarray) -> bool:
 class Shared:
     """Controllers + `world` stores on one device, shards shared in-process."""
 
-    def __init__(self, table, world, page=4096, cache_mb=1, num_ssd=2, device=0, line=0):
+    def __init__(self, table, world, page=4096, cache_mb=1, num_ssd=2, device=0, line=0, admission=True):
         L = gids_abi.lib()
         self.c = ctypes.c_void_p()
         check(L.gids_ctrls_create(ctypes.byref(self.c)))
@@ -46,6 +46,7 @@ class Shared:
             if line:
                 check(L.gids_store_set_cache_line(s, line))
             check(L.gids_store_init_controllers(s, self.c, page, 0, cache_mb, table.size, num_ssd))
+            check(L.gids_store_set_cache_policy(s, 1 if admission else 0, 3))
             self.s.append(s)
         arr = (ctypes.c_void_p * world)(*self.s)
         check(L.gids_store_share_shards(arr, world))
@@ -99,7 +100,7 @@ def test_gather_refused_before_peers_attached():
 def test_in_process_shards_one_gpu(world):
     rows, cdim = 12000, 1024
     t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 21, rows, cdim)
-    sh = Shared(t, world, cache_mb=64)  # 16384 slots per shard: nothing is evicted
+    sh = Shared(t, world, cache_mb=64, admission=False)  # 16384 slots per shard: nothing is evicted
     rng = np.random.default_rng(world)
     try:
         ids = rng.integers(0, rows, size=5000)
