@@ -71,10 +71,11 @@ CONFIGS = {
                cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None, line=512),
 }
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per gathered row of gather_kernel, from one
-# ncu --set full capture of a small case of the same config with the same hit/fill mix
-# (config 2: 4M nodes, 2 GB cache, batch 512 -> 3.182 GB over 366,578 rows); a full launch's
-# traffic is this times its rows. Configs without such a capture report null.
-TRAFFIC_PER_ROW = {"c2": 3.182e9 / 366578}
+# ncu --set full capture of a small case of the same config, after the same cache warm-up
+# (config 2: 4M nodes, 2 GB cache, batch 512, 16 warm-up minibatches -> 2.386 GB over 366,578
+# rows at 41 % hits; the full run has 34 %); a full launch's traffic is this times its rows.
+# Configs without such a capture report null.
+TRAFFIC_PER_ROW = {"c2": 2.386e9 / 366578}
 KIND = {"float32": 1, "float16": 2}
 TDTYPE = {"float32": torch.float32, "float16": torch.float16}
 ESIZE = {"float32": 4, "float16": 2}
