@@ -192,42 +192,82 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
-def make_batches(cfg, n_batches, rank, device, with_pins=False):
+def batch_stream(cfg, n_batches, rank, device):
     """Input-node ids of n_batches minibatches from the seeded graph and
-    sampler, and (with_pins) the PageRank pin list of the constant CPU buffer."""
-    from GIDS.synthetic import NeighborSampler, SyntheticGraph, pagerank_pin_list, seed_batches
+    sampler, produced lazily (one neighbour-sampling pass per next())."""
+    from GIDS.synthetic import NeighborSampler, SyntheticGraph, seed_batches
 
-    t0 = time.time()
     if cfg["hetero"]:
         from GIDS.synthetic import HeteroNeighborSampler, HeteroSyntheticGraph
 
         h = cfg["hetero"]
         hg = HeteroSyntheticGraph(h["types"], h["relations"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
         hs = HeteroNeighborSampler(hg, cfg["fanouts"], seed=sampler_seed(rank))
-        seeds = seed_batches(h["types"][h["seed_type"]], cfg["batch"], n_batches, sampler_seed(rank), device=device)
-        out = [hs.sample({h["seed_type"]: sd})[0] for sd in seeds]
-        del hg, hs
-        if device != "cpu":
-            torch.cuda.synchronize()
-        return (out, None, time.time() - t0) if with_pins else (out, time.time() - t0)
+        for sd in seed_batches(h["types"][h["seed_type"]], cfg["batch"], n_batches, sampler_seed(rank), device=device):
+            yield hs.sample({h["seed_type"]: sd})[0]
+        return
     g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
-    pins = None
-    if with_pins and cfg["cpu_pin_frac"] > 0:
-        pins = pagerank_pin_list(g, cfg["cpu_pin_frac"])
     s = NeighborSampler(g, cfg["fanouts"], seed=sampler_seed(rank))
-    seeds = seed_batches(cfg["nodes"], cfg["batch"], n_batches, sampler_seed(rank), device=device,
-                         zipf_alpha=cfg["seed_zipf"])
-    out = []
-    for sd in seeds:
-        inp, _ = s.sample(sd)
-        out.append(inp)
-    del g, s
+    for sd in seed_batches(cfg["nodes"], cfg["batch"], n_batches, sampler_seed(rank), device=device,
+                           zipf_alpha=cfg["seed_zipf"]):
+        yield s.sample(sd)[0]
+
+
+class SideStreamBatches:
+    """Iterator of [input_nodes] whose sampling runs on `side`; the consumer's
+    stream waits for each batch with an event, so a batch is sampled while
+    the consumer's previous work (the gather) is still running."""
+
+    def __init__(self, gen, side, main):
+        self.gen, self.side, self.main = gen, side, main
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        with torch.cuda.stream(self.side):
+            b = next(self.gen)
+            ev = torch.cuda.Event()
+            ev.record(self.side)
+        self.main.wait_event(ev)
+        for t in (b.values() if isinstance(b, dict) else [b]):
+            t.record_stream(self.main)
+        return [b]
+
+
+def time_sampler(cfg, n, rank, device, side):
+    """Milliseconds per minibatch of the neighbour sampler alone, on `side`."""
+    gen = batch_stream(cfg, n + 1, rank, device)
+    with torch.cuda.stream(side):
+        next(gen)  # graph setup and first-call costs stay out of the figure
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            next(gen)
+        torch.cuda.synchronize()
+    return (time.perf_counter() - t0) / n * 1e3
+
+
+def make_batches(cfg, n_batches, rank, device, with_pins=False):
+    """Input-node ids of n_batches minibatches from the seeded graph and
+    sampler, and (with_pins) the PageRank pin list of the constant CPU buffer."""
+    from GIDS.synthetic import SyntheticGraph, pagerank_pin_list
+
+    t0 = time.time()
+    pins = None
+    if with_pins and cfg["cpu_pin_frac"] > 0 and not cfg["hetero"]:
+        pins = pagerank_pin_list(SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device),
+                                 cfg["cpu_pin_frac"])
+    out = list(batch_stream(cfg, n_batches, rank, device))
     if device != "cpu":
         torch.cuda.synchronize()
     if with_pins:
         return out, pins, time.time() - t0
     return out, time.time() - t0
 
+
+# NVLink peer-read bound (GB/s per direction per GPU): a peer copy measured on this pool's B200s
+NVLINK_PEER_GBS = 770.0
 
 # untimed cache warm-up, in cache-sizes of line references
 CACHE_WARMUP_CACHES = 12
@@ -361,7 +401,8 @@ def run_ours(args, cfg, dist: Dist):
                   synchronous=False, shard_cache=shared and not args.no_shard, window_buffer=cfg["wb"] > 0,
                   wb_size=max(1, cfg["wb"]), cache_line=cfg["line"] or None,
                   heterograph=cfg["hetero"] is not None, heterograph_map=hmap,
-                  cache_admission=POLICIES[args.policy][0], cache_ref_max=POLICIES[args.policy][1])
+                  cache_admission=POLICIES[args.policy][0], cache_ref_max=POLICIES[args.policy][1],
+                  gather_blocks=args.gather_blocks)
     t_store = time.time() - t0
     if not shared:
         t0 = time.time()
@@ -475,6 +516,7 @@ def run_ours(args, cfg, dist: Dist):
         if isinstance(feat, dict):
             feat = feat[max(feat, key=lambda k: feat[k].shape[0])]
         checks += float(feat[-1, -1].item())  # D2H read of the step's result
+        del batch, feat  # the step is done with its features, as a training step would be
     e1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -483,6 +525,37 @@ def run_ours(args, cfg, dist: Dist):
     t_e2e = e0.elapsed_time(e1) / 1e3
     st_e2e = bam.get_stats()
     rows_e2e = st_e2e["rows"]
+
+    # ---- loader: the sampler on a side stream overlapped with the gather, fresh
+    #      minibatches (other sampler seeds); wall time with the device idle at both ends
+    loader = None
+    if not args.no_loader:
+        side = torch.cuda.Stream(device)
+        sample_ms = time_sampler(cfg, args.steps, dist.rank + 3571, device, side)
+        g.window_buffer.clear()
+        g.wb_init = False
+        lit = SideStreamBatches(batch_stream(cfg, args.steps + wb, dist.rank + 3571, device), side, stream)
+        if wb:
+            g.fill_wb(lit, wb)
+            g.wb_init = True
+        torch.cuda.synchronize()
+        bam.reset_stats()
+        dist.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            g.fetch_feature(dim, lit, device)
+        torch.cuda.synchronize()
+        t_loader = time.perf_counter() - w0
+        dist.barrier()
+        st_l = bam.get_stats()
+        t_loader_max = dist.max(t_loader)
+        loader = {"minibatches_per_s": round(dist.sum(args.steps) / t_loader_max, 3),
+                  "gathered_gbs": round(dist.sum(st_l["rows"]) * row_bytes / 1e9 / t_loader_max, 3),
+                  "sampler_ms_per_minibatch": round(sample_ms, 2),
+                  "gather_ms_per_minibatch": None,
+                  "note": "wall time of fetch_feature over a lazy sampler whose neighbour sampling runs on a "
+                          "second CUDA stream while the previous minibatch's gather runs"}
 
     # ---- aggregate over ranks
     t_val_max = dist.max(t_val)
@@ -498,22 +571,29 @@ def run_ours(args, cfg, dist: Dist):
     r_host = (st["bytes_miss"] + st["bytes_bypass"] + st["bytes_cpu"]) / n_launch
     r_hbm_src = st["bytes_hit"] / n_launch
     alg_hbm = r_hbm_src + rows_l * row_bytes + 8 * rows_l  # source reads of hits + output writes + ids
-    t_star = max(alg_hbm / (hbm_peak * 1e9), r_host / (host_peak * 1e9))
-    bound = "hbm" if alg_hbm / (hbm_peak * 1e9) >= r_host / (host_peak * 1e9) else "host_link"
-    if bound == "hbm":
-        achieved, peak, unit_peak = alg_hbm / t_launch / 1e9, hbm_peak, "GB/s"
-    else:
-        achieved, peak, unit_peak = r_host / t_launch / 1e9, host_peak, "GB/s"
+    r_peer = st.get("bytes_peer", 0) / n_launch  # hit bytes read from other ranks' shards over NVLink
+    terms = {"hbm": (alg_hbm, hbm_peak), "host_link": (r_host, host_peak)}
+    if dist.world > 1:
+        terms["nvlink"] = (r_peer, NVLINK_PEER_GBS)
+    bound = max(terms, key=lambda k: terms[k][0] / terms[k][1])
+    t_star = terms[bound][0] / (terms[bound][1] * 1e9)
+    achieved, peak, unit_peak = terms[bound][0] / t_launch / 1e9, terms[bound][1], "GB/s"
     acc = max(1, st["access"])
     roofline = {
         "bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": unit_peak,
         "frac": round(t_star / t_launch, 4),
         "traffic": (int(TRAFFIC_PER_ROW[args.config] * rows_l) if args.config in TRAFFIC_PER_ROW and not args.nodes
-                    else None),
-        "peak_source": (hbm_src + " (of measured)") if bound == "hbm" else
-        "pinned host->device copy measured live in this run, all ranks copying at once (of measured)",
-        "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss)/BW_host); frac = T*/T_launch",
+                    and dist.world == 1 else None),
+        "peak_source": {"hbm": hbm_src + " (of measured)",
+                        "host_link": "pinned host->device copy measured live in this run, all ranks copying at "
+                                     "once (of measured)",
+                        "nvlink": "peer copy per direction per GPU measured on this pool's B200s (of measured, "
+                                  "not live)"}[bound],
+        "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss)/BW_host, R*n_peer/BW_nvlink); "
+                 "frac = T*/T_launch",
         "t_launch_ms": round(t_launch * 1e3, 3), "t_star_ms": round(t_star * 1e3, 3),
+        "nvlink": {"alg_bytes_per_launch": int(r_peer), "achieved_gbs": round(r_peer / t_launch / 1e9, 1),
+                   "peak_gbs": NVLINK_PEER_GBS} if dist.world > 1 else None,
         "hbm": {"alg_bytes_per_launch": int(alg_hbm), "achieved_gbs": round(alg_hbm / t_launch / 1e9, 1),
                 "peak_gbs": hbm_peak},
         "host_link": {"alg_bytes_per_launch": int(r_host), "achieved_gbs": round(r_host / t_launch / 1e9, 2),
@@ -524,6 +604,8 @@ def run_ours(args, cfg, dist: Dist):
     }
     gb_val = rows_val_all * row_bytes / 1e9
     value = gb_val / t_val_max
+    if loader is not None:
+        loader["gather_ms_per_minibatch"] = round(t_val_max / len(dev_ids) * 1e3, 2)
     e2e_value = rows_e2e_all * row_bytes / 1e9 / t_e2e_max
     result = {
         "metric": "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs",
@@ -546,13 +628,15 @@ def run_ours(args, cfg, dist: Dist):
                    "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
                    "window_buffer_depth": wb,
                    "cache_policy": args.policy,
-                   "cache_warmup_minibatches": n_cw},
+                   "cache_warmup_minibatches": n_cw,
+                   "gather_grid_cap": args.gather_blocks or None},
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "api": "GIDS.fetch_feature",
                 "h2d_bytes_per_step": int(np.mean([nrows(b) * 8 for b in e2e_batches])),
                 "d2h_bytes_per_step": esize, "wall_s": round(wall_e2e, 3),
                 "minibatches_per_s": round(dist.sum(len(e2e_batches)) / t_e2e_max, 3),
                 "mix": {"hit": round(st_e2e["hit"] / max(1, st_e2e["access"]), 4)}},
+        "loader": loader,
         "gpu_launches": int(launches) + (len(dev_ids) if wb else 0),
         "clocks": clk,
         "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1),
@@ -606,6 +690,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-shard", action="store_true", help="N>1: independent caches instead of one sharded cache")
     ap.add_argument("--cache-line", type=int, default=-1, help="cache line bytes (0 = the page; -1 = the config's)")
+    ap.add_argument("--no-loader", action="store_true", help="skip the loader (sampler overlapped) measurement")
+    ap.add_argument("--gather-blocks", type=int, default=0, help="cap on the gather kernel's grid (0: all resident)")
     ap.add_argument("--cache-warmup", type=int, default=-1,
                     help="untimed minibatches (other sampler seeds) gathered before the warm-up steps; -1: "
                          "enough for about 12 cache-sizes of line references, at most 60")

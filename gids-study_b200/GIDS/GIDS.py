@@ -76,14 +76,16 @@ class GIDS:
     (default True) inserts a line on its second miss within a window of twice
     the cache's slots, so lines touched once do not evict lines touched often;
     ``cache_ref_max`` (default 3) is the clock counter ceiling (1 = the
-    second-chance clock). Neither changes what is gathered.
+    second-chance clock). Neither changes what is gathered. ``gather_blocks``
+    caps the gather kernel's grid (0: every block the GPU holds at once), so a
+    gather bound by the host link leaves SMs to kernels on other streams.
     """
 
     def __init__(self, page_size=4096, off=0, cache_dim=1024, num_ele=300 * 1000 * 1000 * 1024, num_ssd=1,
                  ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
                  long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
                  ssd_path=None, synchronous=False, shard_cache=False, process_group=None, cache_line=None,
-                 cache_admission=True, cache_ref_max=3):
+                 cache_admission=True, cache_ref_max=3, gather_blocks=0):
         if dtype is None:
             dtype = torch.int64 if long_type else torch.float32
         if dtype not in _STORE_CLASSES:
@@ -144,6 +146,8 @@ class GIDS:
             self._attach_peer_shards()
         self.BAM_FS.set_row_layout(cache_dim)
         self.BAM_FS.set_cache_policy(bool(cache_admission), int(cache_ref_max))
+        if gather_blocks:
+            self.BAM_FS.set_gather_blocks(int(gather_blocks))
         self.BAM_FS.set_synchronous(bool(synchronous))
         self.synchronous = bool(synchronous)
 

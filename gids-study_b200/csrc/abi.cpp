@@ -211,6 +211,13 @@ int gids_store_set_cache_policy(gids_store_t* s, int admission, uint32_t ref_max
   });
 }
 
+int gids_store_set_gather_blocks(gids_store_t* s, uint32_t max_blocks) {
+  return guarded([&] {
+    NEED(s);
+    s->s.set_gather_blocks(max_blocks);
+  });
+}
+
 int gids_store_debug_mark_busy(gids_store_t* s, uint64_t line) {
   return guarded([&] {
     NEED(s);

@@ -188,6 +188,8 @@ class FeatureStore {
   }
   // replacement policy: admission on the second miss, clock counter ceiling
   void set_cache_policy(bool admission, uint32_t ref_max) { check(gids_store_set_cache_policy(s(), admission ? 1 : 0, ref_max)); }
+  // cap on the gather's grid (0: every resident block)
+  void set_gather_blocks(uint32_t n) { check(gids_store_set_gather_blocks(s(), n)); }
   py::bytes ipc_handle() {
     char h[64];
     check(gids_store_ipc_handle(s(), h, sizeof(h)));
@@ -310,6 +312,7 @@ void bind_store(py::module_& m, const char* name) {
       .def("set_sharding", &S::set_sharding, py::arg("world"), py::arg("rank"))
       .def("set_cache_line", &S::set_cache_line, py::arg("bytes"))
       .def("set_cache_policy", &S::set_cache_policy, py::arg("admission"), py::arg("ref_max"))
+      .def("set_gather_blocks", &S::set_gather_blocks, py::arg("max_blocks"))
       .def("ipc_handle", &S::ipc_handle)
       .def("open_peers", &S::open_peers)
       .def("set_synchronous", &S::set_synchronous, R())

@@ -423,14 +423,21 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         todo &= ~grp;
         const DevShard& V = a.c.sh[tgt];
         for (uint32_t round = 0; grp && round < a.sweep_limit; round++) {
+          // the hand passes only as many slots as there are owners to place,
+          // doubling per round when candidates are still in use: passing more
+          // would spend chances of slots no fill needed and age the cache
+          // faster than lines are replaced
+          const uint32_t m = min(32u, (uint32_t)__popc(grp) << min(round, 5u));
           unsigned long long base = 0;
-          if (lane == 0) base = atom_add_relaxed<SYS>(V.clock, 32ull);
+          if (lane == 0) base = atom_add_relaxed<SYS>(V.clock, (unsigned long long)m);
           base = __shfl_sync(0xffffffffu, base, 0);
+          const bool looks = (uint32_t)lane < m;
           const uint64_t s = (base + (uint64_t)lane) % a.c.n_slots;
-          const unsigned long long q = ld_relaxed<SYS>(V.slot_page + s);
+          const unsigned long long q = looks ? ld_relaxed<SYS>(V.slot_page + s) : 0ull;
           bool cand = false;
           unsigned long long expect = 0;
-          if (q == SLOT_EMPTY) {
+          if (!looks) {
+          } else if (q == SLOT_EMPTY) {
             cand = true;
           } else if (const unsigned char rr = V.slot_ref[s]) {
             V.slot_ref[s] = rr - 1;  // the clock hand spends one chance

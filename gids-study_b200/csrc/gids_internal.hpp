@@ -237,6 +237,7 @@ class Store {
   uint32_t ref_max = 3;
   uint64_t refs_since_seen_reset = 0;
   void set_policy(bool admit, uint32_t ref_ceiling);
+  void set_gather_blocks(uint32_t n);
   // gather with the page cache in the library's static no-allocation scratch (noalloc.cu)
   void read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
                     cudaStream_t st);
@@ -310,6 +311,7 @@ class Store {
   uint64_t launches = 0;
   void fold_events(bool wait);
   int grid_blocks[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  uint32_t max_blocks = 0;  // cap on a gather's grid (0: the resident maximum)
   std::mutex mu;
 
  private:

@@ -327,6 +327,11 @@ void Store::set_policy(bool admit, uint32_t ref_ceiling) {
   ref_max = ref_ceiling;
 }
 
+void Store::set_gather_blocks(uint32_t n) {
+  std::lock_guard<std::mutex> lk(mu);
+  max_blocks = n;
+}
+
 void Store::set_cache_line(uint32_t bytes) {
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(!initialized, GIDS_E_STATE, "set_cache_line after init_controllers");
@@ -433,7 +438,9 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
     a.total_chunks = chunks;
     const int vi = vec == 16 ? 0 : vec == 8 ? 1 : vec == 4 ? 2 : 3;
     const uint64_t want_blocks = (chunks + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
-    const int grid = (int)std::min<uint64_t>(want_blocks, (uint64_t)grid_blocks[world > 1 ? 1 : 0][vi]);
+    uint64_t cap = (uint64_t)grid_blocks[world > 1 ? 1 : 0][vi];
+    if (max_blocks) cap = std::min<uint64_t>(cap, max_blocks);
+    const int grid = (int)std::min<uint64_t>(want_blocks, cap);
     EvPair ev;
     if (!ev_free.empty()) {
       ev = ev_free.back();

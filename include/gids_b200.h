@@ -127,6 +127,11 @@ GIDS_API int gids_store_set_cache_line(gids_store_t *s, uint32_t bytes);
  * to ref_max and the clock hand spends one per pass (1 = second chance).
  * Results do not depend on the policy; only hit ratios do. */
 GIDS_API int gids_store_set_cache_policy(gids_store_t *s, int admission, uint32_t ref_max);
+/* Largest grid of one gather launch, in blocks of 256 threads (no reference
+ * counterpart). 0 (default): every block the GPU can hold at once (2 per SM).
+ * A gather bound by the host link keeps the link busy with fewer blocks and
+ * leaves SMs to kernels on other streams (a sampler, the training step). */
+GIDS_API int gids_store_set_gather_blocks(gids_store_t *s, uint32_t max_blocks);
 /* Bounded waits (no reference counterpart; the reference spins forever,
  * page_cache_backup.h:1389-1401): a gather polls a line that another warp or
  * GPU is filling at most `polls` times (exponential back-off, 32 ns to 2 us),

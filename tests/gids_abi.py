@@ -71,6 +71,7 @@ def lib():
             "gids_store_set_cache_line": (i32, [vp, u32]),
             "gids_store_set_wait_limit": (i32, [vp, u32]),
             "gids_store_set_cache_policy": (i32, [vp, i32, u32]),
+            "gids_store_set_gather_blocks": (i32, [vp, u32]),
             "gids_store_debug_mark_busy": (i32, [vp, u64]),
             "gids_store_ipc_handle": (i32, [vp, vp, ctypes.c_size_t]),
             "gids_store_open_peers": (i32, [vp, vp, i32]),
