@@ -86,3 +86,18 @@ def test_pagerank_pin_list_matches_dense_restatement():
     top = np.argsort(-pv, kind="stable")[: int(N * 0.02)]
     assert set(top.tolist()) == set(pins.tolist())
     assert pv[pins[0].item()] == pv.max()
+
+
+def test_bench_batch_stream_is_the_batch_list():
+    """bench.py's lazy sampler stream yields the same minibatches as its list
+    form (the timed steps and the loader measurement draw from the same law)."""
+    import bench
+
+    cfg = dict(bench.CONFIGS["c1"], nodes=20000, batch=64)
+    lst, _ = bench.make_batches(cfg, 3, 0, "cpu")
+    lazy = list(bench.batch_stream(cfg, 3, 0, "cpu"))
+    assert len(lst) == len(lazy) == 3
+    for a, b in zip(lst, lazy):
+        assert torch.equal(a, b)
+    other = list(bench.batch_stream(cfg, 1, 1, "cpu"))[0]
+    assert not torch.equal(other, lst[0])
