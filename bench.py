@@ -614,9 +614,7 @@ def run_ours(args, cfg, dist: Dist):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt],
         "data": "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)",
         "minibatches_per_s": round(steps_all / t_val_max, 3),
-        "config": {"workload": f"{args.config}: {cfg['nodes']} nodes, {dt} x {dim} ({range_bytes / 1e9:.1f} GB range), "
-                               f"{page} B pages over {cfg['ssds']} emulated SSDs, {cfg['cache_mb'] // 1024} GB cache/GPU "
-                               f"in {geo.get('cache_line', page)} B lines, fanout {cfg['fanouts']}, batch {cfg['batch']}",
+        "config": {"workload": workload_name(args, cfg),
                    "global_batch": cfg["batch"] * dist.world,
                    "parallelism": f"dp{dist.world} (independent trainers" +
                                   (", page cache sharded by page id over NVLink)" if g.world > 1 else ")"),
@@ -647,6 +645,15 @@ def run_ours(args, cfg, dist: Dist):
     return result, batches
 
 
+def workload_name(args, cfg) -> str:
+    """The workload as both arms name it in their JSON line."""
+    dt, dim, page = cfg["dtype"], cfg["dim"], cfg["page"]
+    range_gb = cfg["nodes"] * dim * ESIZE[dt] / 1e9
+    return (f"{args.config}: {cfg['nodes']} nodes, {dt} x {dim} ({range_gb:.1f} GB range), {page} B pages over "
+            f"{cfg['ssds']} emulated SSDs, {cfg['cache_mb'] // 1024} GB cache/GPU in {cfg['line'] or page} B lines, "
+            f"fanout {cfg['fanouts']}, batch {cfg['batch']}")
+
+
 def run_reference(args, cfg, dist: Dist):
     """The reference's CPU gather (the mmap baseline) on the host cores."""
     if dist.rank != 0:
@@ -667,7 +674,8 @@ def run_reference(args, cfg, dist: Dist):
         "ms_per_step": round(res["seconds"] / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt], "data": "synthetic",
         "minibatches_per_s": round(res["minibatches_per_s"], 3),
-        "config": {"workload": args.config, "global_batch": cfg["batch"], "parallelism": "host cores"},
+        "config": {"workload": workload_name(args, cfg), "global_batch": cfg["batch"],
+                   "parallelism": "host cores (rank 0 only)"},
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": res["cores"], "kind": "port",
                          "sample": res["sample"]},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
