@@ -31,6 +31,8 @@
 // bit per slot (second chance) and every spin bounded.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "gids_internal.hpp"
 
 namespace gids {
@@ -215,6 +217,138 @@ __device__ __forceinline__ void copy_segments(const SegDesc* sd, int nseg, int l
   }
 }
 
+// ------------------------------------------------------------ TMA bulk copies
+// Segments whose source is a cache slot (a hit, or a line another warp filled)
+// are moved HBM -> shared -> output by the tensor memory accelerator rather
+// than through registers: one lane per warp issues `cp.async.bulk` loads into
+// the warp's ring of TMA_STAGES shared-memory stages (completion counted in
+// bytes on each stage's mbarrier) and bulk stores from each completed stage to
+// the output rows. Bytes in flight are then bounded by shared memory instead
+// of the registers the lookups and fills already need. Only the 16-byte-vector
+// kernels use it (bulk copies need 16-byte aligned addresses and sizes).
+constexpr int TMA_STAGES = 3;
+constexpr uint32_t TMA_STAGE_BYTES = 4096;
+constexpr uint32_t TMA_WAIT_LIMIT = 1u << 22;  // mbarrier polls before a stage is given up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(unsigned long long* b) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity) {
+  uint32_t ok = 0;
+  for (uint32_t it = 0; it < TMA_WAIT_LIMIT && !ok; it++)
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_load(char* sdst, const char* gsrc, uint32_t bytes, unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(sdst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_store(char* gdst, const char* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
+
+// One warp's pipeline over n segments, run by one lane, its state in shared
+// memory: stage k of the ring holds the k-th 4 KB of the segments'
+// concatenation (pieces of several small segments share a stage). issue()
+// starts the loads of the first stages; drain() completes every stage in
+// order, stores it to the output, and refills it.
+struct TmaPipe {
+  const SegDesc* sd;
+  char* ring;
+  unsigned long long* bar;
+  int n, jp, jc, issued, done;
+  uint32_t op, oc;
+  uint32_t sb[TMA_STAGES];
+  uint32_t phase;  // parity of each stage's next completion
+  int live;        // cleared for good if a stage ever fails to complete
+
+  __device__ __forceinline__ bool pack(int s) {
+    if (jp >= n) return false;
+    uint32_t fill = 0;
+    int j = jp;
+    uint32_t o = op;
+    while (j < n && fill < TMA_STAGE_BYTES) {
+      const uint32_t take = min(sd[j].len - o, TMA_STAGE_BYTES - fill);
+      fill += take;
+      o += take;
+      if (o == sd[j].len) {
+        j++;
+        o = 0;
+      }
+    }
+    sb[s] = fill;
+    mbar_expect_tx(bar + s, fill);
+    char* const dst = ring + (size_t)s * TMA_STAGE_BYTES;
+    fill = 0;
+    while (jp < n && fill < TMA_STAGE_BYTES) {
+      const uint32_t take = min(sd[jp].len - op, TMA_STAGE_BYTES - fill);
+      bulk_load(dst + fill, sd[jp].src + op, take, bar + s);
+      fill += take;
+      op += take;
+      if (op == sd[jp].len) {
+        jp++;
+        op = 0;
+      }
+    }
+    return true;
+  }
+  __device__ __forceinline__ void issue(const SegDesc* segs, int count, char* r, unsigned long long* b) {
+    sd = segs;
+    n = count;
+    ring = r;
+    bar = b;
+    jp = jc = issued = done = 0;
+    op = oc = 0;
+    // the previous chunk's bulk stores may still be reading the ring
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    // the slots were written through the generic proxy (fills, made visible by
+    // the acquire on their page-table words); order them before the bulk reads
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    for (int s = 0; s < TMA_STAGES && pack(s); s++) issued++;
+  }
+  // false: a stage did not complete within the limit (the caller copies the
+  // segments again another way)
+  __device__ __forceinline__ bool drain() {
+    while (done < issued) {
+      const int s = done % TMA_STAGES;
+      if (!mbar_wait(bar + s, (phase >> s) & 1u)) return false;
+      phase ^= 1u << s;
+      const char* const src = ring + (size_t)s * TMA_STAGE_BYTES;
+      uint32_t used = 0;
+      while (used < sb[s]) {
+        const uint32_t take = min(sd[jc].len - oc, sb[s] - used);
+        bulk_store(sd[jc].dst + oc, src + used, take);
+        used += take;
+        oc += take;
+        if (oc == sd[jc].len) {
+          jc++;
+          oc = 0;
+        }
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      done++;
+      if (jp < n) {
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the stage has been read out
+        if (pack(s)) issued++;
+      }
+    }
+    return true;
+  }
+};
+
 // Whole-page fill from the backing store into a cache slot (16-byte vectors;
 // pages are >= 512 B, power-of-two sized, and page-aligned on both sides).
 // With FWD, the segments of the rows in `mem` (lanes whose rows read this
@@ -293,11 +427,22 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
   __shared__ unsigned long long cnt_sh[WARPS][K_N];  // warp-private counters
   __shared__ unsigned char fill_lane[WARPS][8];      // owner lanes of one fill batch
   __shared__ unsigned char gate_sh[GIDS_MAX_WORLD];   // shard filters first misses (full, admission on)
+  __shared__ __align__(8) unsigned long long tma_bar[WARPS][TMA_STAGES];
+  __shared__ TmaPipe tma_pipe_sh[WARPS];
+  extern __shared__ __align__(128) char tma_ring_sh[];  // WARPS x TMA_STAGES x 4 KB (VEC == 16)
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   SegDesc* sd = seg_sh[wib];
   unsigned long long* acc = cnt_sh[wib];
   if (lane < K_N) acc[lane] = 0;
+  TmaPipe& pipe = tma_pipe_sh[wib];
+  if (VEC == 16 && lane == 0) {
+    for (int s = 0; s < TMA_STAGES; s++) mbar_init(&tma_bar[wib][s]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    pipe.phase = 0;
+    pipe.live = 1;
+  }
+  __syncwarp();
   // a shard admits every miss until its clock hand has gone round once (the
   // cache is full); read once per block, a stale "not full" only admits more
   if (threadIdx.x < GIDS_MAX_WORLD)
@@ -626,11 +771,36 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       dst = orow + s0;
       len = s1 - s0;
     }
-    const unsigned has = __ballot_sync(0xffffffffu, len != 0);
-    const int pos = __popc(has & ((1u << lane) - 1u));
-    if (len) sd[pos] = SegDesc{src, dst, len, 0u};
+    // slot-sourced segments go to the TMA pipeline (from the end of the table),
+    // the rest (host, constant CPU buffer, zero rows) to the vector copy
+    const bool via_tma = VEC == 16 && len && seg_ok && !forwarded && gcls != CLS_BYPASS && pipe.live;
+    const unsigned tm = __ballot_sync(0xffffffffu, via_tma);
+    const unsigned has = __ballot_sync(0xffffffffu, len != 0 && !via_tma);
+    const unsigned below = (1u << lane) - 1u;
+    if (via_tma)
+      sd[31 - __popc(tm & below)] = SegDesc{src, dst, len, 0u};
+    else if (len)
+      sd[__popc(has & below)] = SegDesc{src, dst, len, 0u};
     __syncwarp();
-    copy_segments<VEC>(sd, __popc(has), lane);
+    const int nt = __popc(tm);
+    if (VEC == 16 && nt && lane == 0)
+      pipe.issue(sd + (32 - nt), nt, tma_ring_sh + (size_t)wib * TMA_STAGES * TMA_STAGE_BYTES, tma_bar[wib]);
+    copy_segments<VEC>(sd, __popc(has), lane);  // overlaps the bulk loads in flight
+    if (VEC == 16 && nt) {
+      bool ok = true;
+      if (lane == 0) ok = pipe.drain();
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        // a bulk load did not complete: record it, stop using the ring, and copy
+        // this chunk's slot segments through registers (rewriting any bytes
+        // the pipeline already stored with the same values)
+        if (lane == 0) {
+          pipe.live = 0;
+          *reinterpret_cast<volatile int*>(a.host_err) = 2;
+        }
+        copy_segments<VEC>(sd + (32 - nt), nt, lane);
+      }
+    }
     __syncwarp();
 
     // ---- release, clock reference bit, window-buffer consumption
@@ -680,6 +850,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 
   __syncwarp();
   if (lane == 0) {
+    if (VEC == 16) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // the output's bulk stores
 #pragma unroll
     for (int i = 0; i < K_N; i++)
       if (acc[i]) atomicAdd(a.stats + kStatMap[i], acc[i]);
@@ -707,10 +878,26 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
 
 }  // namespace
 
+constexpr size_t kTmaRingBytes = (size_t)WARPS * TMA_STAGES * TMA_STAGE_BYTES;
+
+// the 16-byte-vector kernels take the TMA ring as dynamic shared memory
+template <bool SYS>
+static void allow_tma_ring() {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(gather_kernel<16, SYS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaRingBytes);
+  });
+  GIDS_CUDA(err);
+}
+
 template <bool SYS>
 static void launch_scoped(const GatherArgs& a, int vec, int grid, cudaStream_t st) {
   switch (vec) {
-    case 16: gather_kernel<16, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
+    case 16:
+      allow_tma_ring<SYS>();
+      gather_kernel<16, SYS><<<grid, GATHER_THREADS, kTmaRingBytes, st>>>(a);
+      break;
     case 8: gather_kernel<8, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
     case 4: gather_kernel<4, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
     case 2: gather_kernel<2, SYS><<<grid, GATHER_THREADS, 0, st>>>(a); break;
@@ -730,7 +917,10 @@ template <bool SYS>
 static int occupancy(int vec) {
   int n = 0;
   switch (vec) {
-    case 16: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<16, SYS>, GATHER_THREADS, 0)); break;
+    case 16:
+      allow_tma_ring<SYS>();
+      GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<16, SYS>, GATHER_THREADS, kTmaRingBytes));
+      break;
     case 8: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<8, SYS>, GATHER_THREADS, 0)); break;
     case 4: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<4, SYS>, GATHER_THREADS, 0)); break;
     case 2: GIDS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_kernel<2, SYS>, GATHER_THREADS, 0)); break;

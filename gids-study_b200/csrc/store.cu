@@ -286,8 +286,11 @@ DevCpuBuf Store::dev_cpu() const {
 }
 
 void Store::check_async_error() {
-  if (h_err && *reinterpret_cast<volatile int*>(h_err)) {
+  const int e = h_err ? *reinterpret_cast<volatile int*>(h_err) : 0;
+  if (e) {
     *reinterpret_cast<volatile int*>(h_err) = 0;
+    if (e == 2)  // the gathered rows are complete: the kernel copied them again without the TMA
+      throw Error(GIDS_E_CUDA, "a TMA bulk copy of the gather did not complete within its wait limit");
     throw Error(GIDS_E_RANGE, "a node id addressed a row outside the feature range (its output row is zero)");
   }
 }

@@ -119,7 +119,7 @@ def test_in_process_shards_one_gpu(world):
         sh.close()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_in_process_shards_churn(world):
     rows, cdim = 12000, 1024
     t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 23, rows, cdim)
