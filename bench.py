@@ -72,10 +72,10 @@ CONFIGS = {
 }
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per gathered row of gather_kernel, from one
 # ncu --set full capture of a small case of the same config, after the same cache warm-up
-# (config 2: 4M nodes, 2 GB cache, batch 512, 16 warm-up minibatches -> 2.386 GB over 366,578
-# rows at 41 % hits; the full run has 34 %); a full launch's traffic is this times its rows.
+# (config 2: 4M nodes, 2 GB cache, batch 512, 16 warm-up minibatches -> 2.495 GB over 366,578
+# rows at 44 % hits; the full run has 39 %); a full launch's traffic is this times its rows.
 # Configs without such a capture report null.
-TRAFFIC_PER_ROW = {"c2": 2.386e9 / 366578}
+TRAFFIC_PER_ROW = {"c2": 2.495e9 / 366578}
 KIND = {"float32": 1, "float16": 2}
 TDTYPE = {"float32": torch.float32, "float16": torch.float16}
 ESIZE = {"float32": 4, "float16": 2}
