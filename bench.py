@@ -601,6 +601,8 @@ def run_ours(args, cfg, dist: Dist):
         "mix": {"hit": round(st["hit"] / acc, 4), "miss": round(st["miss"] / acc, 4),
                 "bypass": round(st["bypass"] / acc, 4), "cpu_rows": st["cpu_rows"],
                 "peer_bytes_frac": round(st.get("bytes_peer", 0) / max(1, st["rows"] * row_bytes), 4)},
+        "counters_per_launch": {k: round(st.get(k, 0) / n_launch, 1)
+                                for k in ("access", "hit", "miss", "read_io", "bypass", "wait_timeouts", "evictions")},
     }
     gb_val = rows_val_all * row_bytes / 1e9
     value = gb_val / t_val_max
