@@ -589,7 +589,7 @@ def run_ours(args, cfg, dist: Dist):
                                      "once (of measured)",
                         "nvlink": "peer copy per direction per GPU measured on this pool's B200s (of measured, "
                                   "not live)"}[bound],
-        "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss)/BW_host, R*n_peer/BW_nvlink); "
+        "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss + n_bypass)/BW_host, R*n_peer/BW_nvlink); "
                  "frac = T*/T_launch",
         "t_launch_ms": round(t_launch * 1e3, 3), "t_star_ms": round(t_star * 1e3, 3),
         "nvlink": {"alg_bytes_per_launch": int(r_peer), "achieved_gbs": round(r_peer / t_launch / 1e9, 1),

@@ -173,7 +173,10 @@ GIDS_API int gids_store_share_shards(gids_store_t *const *stores, int n);
  *   out[i*dim + t] = range[(idx[i] + key_off) * cache_dim + t], t < dim,
  * for i < n. `out` and `idx` are device pointers on the store's GPU; idx is
  * int64. Rows pinned in the constant CPU buffer are read from it. A node id
- * whose row leaves the range gives GIDS_E_RANGE and a zero row. */
+ * whose row leaves the range gives GIDS_E_RANGE and a zero row. GIDS_E_CUDA
+ * with "TMA bulk copy ... wait limit" reports a bulk load of cached lines that
+ * did not complete in time; the rows were then copied another way and are
+ * complete. */
 GIDS_API int gids_read_feature(gids_store_t *s, void *out, const int64_t *idx, int64_t n, int dim, int cache_dim,
                       uint64_t key_off, void *stream);
 /* Replaces read_feature_hetero / read_feature_merged_hetero
