@@ -90,8 +90,11 @@ static void run(const char* policy, int S, int K, double W) {
         int nn = 0, got = 0;
         for (int i = 0; i < no; i++)
           if (own[i] % S == r) need[nn++] = own[i];
-        for (int round = 0; got < nn && round < 64; round++) {
-          int m = warp ? (m32 ? 32 : (nn - got) << (round < 5 ? round : 5)) : 1;
+        /* the warp sweeps give up after 64 rounds, as the kernel does; the sequential clock
+           always places (at most ref_max + 1 passes over the slots) */
+        const int64_t max_rounds = warp ? 64 : (int64_t)(K + 1) * nslots + 1;
+        for (int64_t round = 0; got < nn && round < max_rounds; round++) {
+          int m = warp ? (m32 ? 32 : (nn - got) << (round < 5 ? (int)round : 5)) : 1;
           if (m > 32) m = 32;
           const int64_t base = hand[r];
           hand[r] += m;
