@@ -370,7 +370,7 @@ def run_ours(args, cfg, dist: Dist):
     range_bytes = num_ele * esize
     phys = min(int(cfg["phys_gb"] * 1e9), range_bytes)
     per_ssd = (phys // cfg["ssds"]) // page * page
-    shared = dist.world > 1
+    shared = dist.world > 1 or args.shared_backing
     hmap = None
     if cfg["hetero"]:
         hmap, acc = {}, 0
@@ -701,6 +701,8 @@ def main():
     ap.add_argument("--no-shard", action="store_true", help="N>1: independent caches instead of one sharded cache")
     ap.add_argument("--cache-line", type=int, default=-1, help="cache line bytes (0 = the page; -1 = the config's)")
     ap.add_argument("--no-loader", action="store_true", help="skip the loader (sampler overlapped) measurement")
+    ap.add_argument("--shared-backing", action="store_true",
+                    help="back the emulated SSDs with shared /dev/shm files even on one GPU (as N>1 runs do)")
     ap.add_argument("--gather-blocks", type=int, default=0, help="cap on the gather kernel's grid (0: all resident)")
     ap.add_argument("--cache-warmup", type=int, default=-1,
                     help="untimed minibatches (other sampler seeds) gathered before the warm-up steps; -1: "
@@ -742,7 +744,7 @@ def main():
             print(json.dumps(res), flush=True)
         dist.barrier()
     finally:
-        if dist.world > 1 and dist.rank == 0:  # the shared emulated SSD files
+        if (dist.world > 1 or args.shared_backing) and dist.rank == 0:  # the shared emulated SSD files
             import glob
 
             for f in glob.glob(f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd*"):
