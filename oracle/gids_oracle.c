@@ -1,7 +1,7 @@
 /*
  * gids_oracle.c -- CPU restatement of the GIDS feature-gather path.
  *
- * TEST INFRASTRUCTURE ONLY. This file is the checker: only tests/, the smoke
+ * TEST INFRASTRUCTURE ONLY. It checks results, nothing more: only tests/, the smoke
  * entry point and the bench's CPU-baseline leg load it. The product library
  * never links or calls it.
  *
