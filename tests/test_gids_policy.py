@@ -119,6 +119,31 @@ def test_constructor_forwards_reference_arguments(fake):
     assert g.BAM_FS.calls[1][2:] == (4096, g.off, 7, 1000 * 64, 2)
 
 
+def test_constructor_forwards_extensions(fake):
+    g = fake(cache_admission=False, cache_ref_max=1, gather_blocks=148, cache_line=512)
+    calls = g.BAM_FS.calls
+    assert ("set_cache_line", 512) in calls
+    assert ("set_cache_policy", False, 1) in calls
+    assert ("set_gather_blocks", 148) in calls
+    names = [c[0] for c in calls]
+    # the cache line is fixed before the store is built; the policy and grid cap after
+    assert names.index("set_cache_line") < names.index("init_controllers") < names.index("set_cache_policy")
+    g2 = fake()
+    assert "set_gather_blocks" not in [c[0] for c in g2.BAM_FS.calls]  # 0 keeps the resident maximum
+
+
+def test_bench_arms_name_the_same_workload():
+    import argparse
+
+    import bench
+
+    for name, cfg in bench.CONFIGS.items():
+        w = bench.workload_name(argparse.Namespace(config=name), cfg)
+        assert w.startswith(f"{name}: {cfg['nodes']} nodes") and f"batch {cfg['batch']}" in w
+        assert f"in {cfg['line'] or cfg['page']} B lines" in w
+    assert set(bench.POLICIES) >= {"admit2", "clock"} and bench.POLICIES["clock"] == (False, 1)
+
+
 def test_default_path(fake):
     g = fake()
     bs = batches(3, 50)
