@@ -266,6 +266,9 @@ def make_batches(cfg, n_batches, rank, device, with_pins=False):
     return out, time.time() - t0
 
 
+# per-phase gather timers of a diagnosis build (stats names)
+PHASES = ("ns_lookup", "ns_fill_wait", "ns_copy", "ns_release")
+
 # NVLink peer-read bound (GB/s per direction per GPU): a peer copy measured on this pool's B200s
 NVLINK_PEER_GBS = 770.0
 
@@ -623,6 +626,9 @@ def run_ours(args, cfg, dist: Dist):
                 "peer_bytes_frac": round(st.get("bytes_peer", 0) / max(1, st["rows"] * row_bytes), 4)},
         "counters_per_launch": {k: round(st.get(k, 0) / n_launch, 1)
                                 for k in ("access", "hit", "miss", "read_io", "bypass", "wait_timeouts", "evictions")},
+        # only a library built with GIDS_PHASE_TIMERS=1 counts these (share of warp time per phase)
+        "phase_share": ({k: round(st[k] / max(1, sum(st.get(x, 0) for x in PHASES)), 4) for k in PHASES}
+                        if sum(st.get(x, 0) for x in PHASES) else None),
     }
     gb_val = rows_val_all * row_bytes / 1e9
     value = gb_val / t_val_max

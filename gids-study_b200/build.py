@@ -6,6 +6,7 @@ Outputs (git-ignored, shipped with the source tree):
   BAM_Feature_Store/BAM_Feature_Store*.so  pybind11 module over the C ABI
 
 Usage: python gids-study_b200/build.py [--force]
+       GIDS_PHASE_TIMERS=1 python gids-study_b200/build.py   (diagnosis build: per-phase timers)
 """
 from __future__ import annotations
 
@@ -49,13 +50,20 @@ def _run(cmd: list[str]) -> None:
 def build(force: bool = False) -> dict:
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(os.path.dirname(LIB), exist_ok=True)
+    # GIDS_PHASE_TIMERS=1: the diagnosis build (per-phase gather timers in the stats)
+    defines = ["-DGIDS_PHASE_TIMERS"] if os.environ.get("GIDS_PHASE_TIMERS") == "1" else []
+    stamp = os.path.join(BUILD, "defines.txt")
+    if not os.path.exists(stamp) or open(stamp).read() != " ".join(defines):
+        force = True
+        with open(stamp, "w") as f:
+            f.write(" ".join(defines))
     objs = []
     for src in CU_SOURCES:
         s = os.path.join(CSRC, src)
         o = os.path.join(BUILD, src + ".o")
         if force or _stale(o, [s] + HEADERS):
             _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-                  "-Xptxas", "-v", f"-I{INCLUDE}", "-c", s, "-o", o])
+                  "-Xptxas", "-v", *defines, f"-I{INCLUDE}", "-c", s, "-o", o])
         objs.append(o)
     for src in CPP_SOURCES:
         s = os.path.join(CSRC, src)

@@ -217,8 +217,8 @@ class FeatureStore {
     static const char* names[] = {"access",      "hit",       "miss",          "read_io",     "bypass",
                                   "cpu_rows",    "rows",      "wait_timeouts", "bad_ids",     "bytes_hit",
                                   "bytes_miss",  "bytes_bypass", "bytes_cpu",   "evictions",   "launches",
-                                  "bytes_peer"};
-    for (int i = 0; i < 16; i++) d[names[i]] = v[i];
+                                  "bytes_peer",  "ns_lookup", "ns_fill_wait",  "ns_copy",     "ns_release"};
+    for (int i = 0; i < GIDS_STAT_COUNT; i++) d[names[i]] = v[i];
     return d;
   }
   void reset_stats() { check(gids_reset_stats(s())); }

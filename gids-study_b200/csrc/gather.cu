@@ -18,17 +18,20 @@
 //      reference's coalesce_page, page_cache_backup.h:1514-1550) and lets one
 //      leader per page take `count` references on the page-table word;
 //   3. fills the pages it won (BUSY) from the emulated SSDs after a warp-wide
-//      clock sweep for victim slots (32 candidates per atomic on the hand),
-//      and publishes them VALID;
+//      clock sweep for victim slots (as many candidates per atomic on the
+//      hand as it has pages to place), and publishes them VALID; once the
+//      cache is full, a page's first miss in the admission window is read
+//      straight from the backing store instead of being inserted;
 //   4. waits, with a bound, for pages another warp is filling; a wait that
 //      runs out, or a fill that found no slot, reads the page straight from
 //      the backing store (always correct: the store is read-only here);
-//   5. copies all segments of the chunk with 16-byte vector loads/stores,
-//      eight vectors in flight per lane, and drops its page references.
+//   5. copies the chunk's segments: slot-sourced ones through a TMA ring in
+//      shared memory (16-byte kernels), the rest with vector loads/stores,
+//      eight vectors in flight per lane; then drops its page references.
 // The state-word protocol follows range_d_t::acquire_page/release_page
 // (page_cache_backup.h:1278-1403, 1166-1229) with a 64-bit word that also
-// holds the slot; eviction follows find_slot (:2107-2256) with a reference
-// bit per slot (second chance) and every spin bounded.
+// holds the slot; eviction follows find_slot (:2107-2256) with a clock
+// counter per slot (chances left) and every spin bounded.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -413,13 +416,37 @@ __device__ __forceinline__ void wb_consume(unsigned int* w, unsigned int cnt) {
 
 enum {
   K_ROWS, K_CPU, K_BAD, K_ACCESS, K_HIT, K_MISS, K_BYPASS, K_READIO, K_TIMEOUT,
-  K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_BPEER, K_N
+  K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_BPEER,
+#ifdef GIDS_PHASE_TIMERS
+  K_TLOOK, K_TFILL, K_TCOPY, K_TREL,
+#endif
+  K_N
 };
 __constant__ int kStatMap[K_N] = {GIDS_STAT_ROWS,       GIDS_STAT_CPU_ROWS,     GIDS_STAT_BAD_IDS,
                                   GIDS_STAT_ACCESS,     GIDS_STAT_HIT,          GIDS_STAT_MISS,
                                   GIDS_STAT_BYPASS,     GIDS_STAT_READ_IO,      GIDS_STAT_WAIT_TIMEOUT,
                                   GIDS_STAT_BYTES_HIT,  GIDS_STAT_BYTES_MISS,   GIDS_STAT_BYTES_BYPASS,
-                                  GIDS_STAT_BYTES_CPU,  GIDS_STAT_EVICTIONS,    GIDS_STAT_BYTES_PEER};
+                                  GIDS_STAT_BYTES_CPU,  GIDS_STAT_EVICTIONS,    GIDS_STAT_BYTES_PEER,
+#ifdef GIDS_PHASE_TIMERS
+                                  GIDS_STAT_NS_LOOKUP,  GIDS_STAT_NS_FILL,      GIDS_STAT_NS_COPY,
+                                  GIDS_STAT_NS_RELEASE,
+#endif
+};
+
+#ifdef GIDS_PHASE_TIMERS
+// Build option for diagnosis (build.py with GIDS_PHASE_TIMERS=1): lane 0 of
+// every warp adds the nanoseconds (globaltimer) each chunk spends in the
+// lookup, fill-and-wait, copy and release phases to four extra counters. The
+// default build compiles none of it.
+__device__ __forceinline__ unsigned long long phase_clock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define GIDS_PHASE_MARK(v) const unsigned long long v = phase_clock()
+#else
+#define GIDS_PHASE_MARK(v)
+#endif
 
 template <int VEC, bool SYS>
 __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_constant__ GatherArgs a) {
@@ -466,6 +493,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const uint32_t sidx = (uint32_t)lane & seg_mask;
     const bool row_ok = row < T.n;
 
+    GIDS_PHASE_MARK(tph0);
     // ---- 1. node id, range check, constant CPU buffer lookup
     int64_t id = row_ok ? __ldg(T.idx + row) : 0;
     const uint64_t r = (uint64_t)id + T.key_off;
@@ -557,6 +585,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const uint32_t in_pg = seg_ok ? (uint32_t)((b0 + s0) - (p << shift)) : 0u;
     bool forwarded = false;
 
+    GIDS_PHASE_MARK(tph1);
     // ---- 3. fills: per owning shard, a warp-cooperative clock sweep for
     //         victim slots (32 candidates per atomic on that shard's hand)
     unsigned pending = __ballot_sync(0xffffffffu, cls == CLS_OWN);
@@ -750,6 +779,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       }
     }
 
+    GIDS_PHASE_MARK(tph2);
     // ---- 5. segment table and copy
     const int gcls = __shfl_sync(0xffffffffu, cls, leader);
     const unsigned long long gslot = __shfl_sync(0xffffffffu, (unsigned long long)slot, leader);
@@ -803,6 +833,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     }
     __syncwarp();
 
+    GIDS_PHASE_MARK(tph3);
     // ---- release, clock reference bit, window-buffer consumption
     if (took_ref) {
       red_add_release<SYS>(stw, (unsigned long long)(-(long long)cnt));
@@ -813,6 +844,18 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       if (S.wb) wb_consume<SYS>(S.wb + lp, cnt);
     }
 
+#ifdef GIDS_PHASE_TIMERS
+    {
+      const unsigned long long tph4 = phase_clock();
+      if (lane == 0) {
+        acc[K_TLOOK] += tph1 - tph0;
+        acc[K_TFILL] += tph2 - tph1;
+        acc[K_TCOPY] += tph3 - tph2;
+        acc[K_TREL] += tph4 - tph3;
+      }
+      __syncwarp();
+    }
+#endif
     // ---- counters
     if (bad && sidx == 0) *reinterpret_cast<volatile int*>(a.host_err) = 1;
     const unsigned r0 = sidx == 0;

@@ -250,6 +250,13 @@ GIDS_API int gids_flush_cpu_access_count(gids_store_t *s);
 #define GIDS_STAT_EVICTIONS 13
 #define GIDS_STAT_LAUNCHES 14    /* gather kernels launched */
 #define GIDS_STAT_BYTES_PEER 15  /* output bytes copied from another GPU's shard (NVLink) */
+/* Per-phase time of the gather, summed over warps in nanoseconds: lookup,
+ * fills and waits, copy, release. Counted only by a library built with
+ * GIDS_PHASE_TIMERS=1 (a diagnosis build); 0 otherwise. */
+#define GIDS_STAT_NS_LOOKUP 16
+#define GIDS_STAT_NS_FILL 17
+#define GIDS_STAT_NS_COPY 18
+#define GIDS_STAT_NS_RELEASE 19
 #define GIDS_STAT_COUNT 20
 /* Copies the cumulative counters (synchronizes the store's last stream). */
 GIDS_API int gids_get_stats(gids_store_t *s, uint64_t *out, int count);
