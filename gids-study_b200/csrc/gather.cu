@@ -923,15 +923,19 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
 
 constexpr size_t kTmaRingBytes = (size_t)WARPS * TMA_STAGES * TMA_STAGE_BYTES;
 
-// the 16-byte-vector kernels take the TMA ring as dynamic shared memory
+// the 16-byte-vector kernels take the TMA ring as dynamic shared memory; the
+// attribute belongs to the current device, so it is set once per device
 template <bool SYS>
 static void allow_tma_ring() {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    err = cudaFuncSetAttribute(gather_kernel<16, SYS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaRingBytes);
-  });
-  GIDS_CUDA(err);
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  GIDS_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return;
+  GIDS_CUDA(cudaFuncSetAttribute(gather_kernel<16, SYS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kTmaRingBytes));
+  if (dev >= 0 && dev < 64) done[dev] = true;
 }
 
 template <bool SYS>
