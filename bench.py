@@ -77,6 +77,8 @@ CONFIGS = {
 # Configs without such a capture report null.
 TRAFFIC_PER_ROW = {"c2": 2.495e9 / 366578}
 KIND = {"float32": 1, "float16": 2}
+METRIC = "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs"
+DATA = "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)"
 TDTYPE = {"float32": torch.float32, "float16": torch.float16}
 ESIZE = {"float32": 4, "float16": 2}
 
@@ -269,9 +271,6 @@ def make_batches(cfg, n_batches, rank, device, with_pins=False):
 # per-phase gather timers of a diagnosis build (stats names)
 PHASES = ("ns_lookup", "ns_fill_wait", "ns_copy", "ns_release")
 
-# NVLink peer-read bound (GB/s per direction per GPU): a peer copy measured on this pool's B200s
-NVLINK_PEER_GBS = 770.0
-
 # untimed cache warm-up, in cache-sizes of line references
 CACHE_WARMUP_CACHES = 12
 
@@ -311,44 +310,67 @@ def measured_hbm_peak():
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_mmap_gather(cfg, ids_list, seconds_budget, path_dir="/dev/shm", file_gb=8.0, warmup_ids=()):
+def memmap_rows(cfg, file_gb: float) -> tuple[int, str]:
+    """Rows of the CPU-baseline memmap and how ids map onto it. file_gb = 0:
+    the bytes the GPU arm's emulated SSDs physically hold (the whole range when
+    they hold it), capped at 40 % of host RAM; when that is the SSDs' wrap
+    period, row r of the memmap holds exactly what the GPU arm reads for every
+    id = r mod rows, so both arms gather the same bytes."""
+    row_bytes = cfg["dim"] * ESIZE[cfg["dtype"]]
+    logical, physical, wrap = backing_geometry(cfg)
+    try:
+        ram = os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_PHYS_PAGES")
+    except (ValueError, OSError):
+        ram = 64 << 30
+    want = int(file_gb * 1e9) if file_gb > 0 else physical
+    want = min(want, int(0.4 * ram))
+    rows = max(1, min(cfg["nodes"], want // row_bytes))
+    same = (wrap == 0 and rows == cfg["nodes"]) or (wrap and rows * cfg["dim"] == wrap)
+    return rows, ("the same bytes as the GPU arm (its emulated SSDs' wrap period)" if same
+                  else f"ids mod {rows} rows (not the GPU arm's wrap period)")
+
+
+def _flat_ids(cfg, ids):
+    if isinstance(ids, dict):  # heterograph: type-local ids + the type's offset
+        offs, acc = {}, 0
+        for t, n in cfg["hetero"]["types"].items():
+            offs[t] = acc
+            acc += n
+        return np.concatenate([v.cpu().numpy() + offs[k] for k, v in ids.items()])
+    return ids.cpu().numpy()
+
+
+def cpu_mmap_gather(cfg, ids_list, seconds_budget, path_dir="/dev/shm", file_gb=0.0, warmup_ids=(), h2d=True):
     """The reference's mmap baseline gather (torch.index_select on a np.memmap,
     evaluation/dataloader.py:166-169 + homogenous_train_baseline.py:244),
-    timed on the host cores on a bounded sample of the same minibatches.
-    The memmap holds file_gb of rows; ids are taken modulo its row count."""
+    timed on the host cores on a bounded sample of the same minibatches, with
+    the OS page cache warm (the file in /dev/shm). With h2d, the reference's
+    copy of each gathered minibatch to the GPU (homogenous_train_baseline.py:253)
+    is timed after it and reported separately."""
     from oracle import oracle
 
     dim, dt = cfg["dim"], cfg["dtype"]
     row_bytes = dim * ESIZE[dt]
-    rows = max(1, min(cfg["nodes"], int(file_gb * 1e9) // row_bytes))
+    rows, mapping = memmap_rows(cfg, file_gb)
     path = os.path.join(path_dir if os.path.isdir(path_dir) else "/tmp", f"gids_b200_mmap_{os.getpid()}.bin")
+    t0 = time.perf_counter()
     mm = np.memmap(path, dtype=np.dtype(dt), mode="w+", shape=(rows, dim))
     oracle.synth_fill_into(KIND[dt], 1, 0, mm.reshape(-1))
     mm.flush()
     del mm
+    t_fill = time.perf_counter() - t0
     feat = oracle.open_memmap_table(path, np.dtype(dt), rows, dim)
     try:
-        def flat(ids):
-            if isinstance(ids, dict):  # heterograph: type-local ids + the type's offset
-                offs, acc = {}, 0
-                for t, n in cfg["hetero"]["types"].items():
-                    offs[t] = acc
-                    acc += n
-                return np.concatenate([v.cpu().numpy() + offs[k] for k, v in ids.items()])
-            return ids.cpu().numpy()
-
         for ids in warmup_ids:
-            oracle.mmap_index_select(feat, torch.as_tensor(flat(ids) % rows))
+            oracle.mmap_index_select(feat, torch.as_tensor(_flat_ids(cfg, ids) % rows))
         done_rows, t_total, n_batches = 0, 0.0, 0
         t_h2d, h2d_note = 0.0, None
         for ids in ids_list:
-            ids_m = torch.as_tensor(flat(ids) % rows)
+            ids_m = torch.as_tensor(_flat_ids(cfg, ids) % rows)
             t0 = time.perf_counter()
             out = oracle.mmap_index_select(feat, ids_m)
             t_total += time.perf_counter() - t0
-            # the reference then copies the gathered rows to the GPU (homogenous_train_baseline.py:253),
-            # reported separately
-            if h2d_note is None and torch.cuda.is_available():
+            if h2d and h2d_note is None and torch.cuda.is_available():
                 try:
                     torch.cuda.synchronize()
                     t1 = time.perf_counter()
@@ -367,17 +389,104 @@ def cpu_mmap_gather(cfg, ids_list, seconds_budget, path_dir="/dev/shm", file_gb=
         del feat
         os.unlink(path)
     gbs = done_rows * row_bytes / 1e9 / t_total
-    h2d = {}
+    extra = {}
     if t_h2d > 0 and h2d_note is None:
-        h2d = dict(h2d_gbs=round(done_rows * row_bytes / 1e9 / t_h2d, 2),
-                   with_h2d_gbs=round(done_rows * row_bytes / 1e9 / (t_total + t_h2d), 2),
-                   h2d_note="pageable tensor.to('cuda') of each gathered minibatch, as the reference does")
+        extra = dict(h2d_gbs=round(done_rows * row_bytes / 1e9 / t_h2d, 2),
+                     with_h2d_gbs=round(done_rows * row_bytes / 1e9 / (t_total + t_h2d), 2),
+                     h2d_note="pageable tensor.to('cuda') of each gathered minibatch, as the reference does")
     elif h2d_note is not None:
-        h2d = dict(h2d_note=h2d_note)
-    return dict(value=gbs, unit="GB/s", cores=torch.get_num_threads(), kind="port", **h2d,
-                minibatches_per_s=n_batches / t_total, seconds=t_total, steps=n_batches,
+        extra = dict(h2d_note=h2d_note)
+    return dict(value=gbs, unit="GB/s", cores=torch.get_num_threads(), kind="port", **extra,
+                minibatches_per_s=n_batches / t_total, seconds=t_total, steps=n_batches, fill_s=round(t_fill, 1),
                 sample=f"{n_batches} minibatches ({done_rows} rows of {row_bytes} B) gathered by torch.index_select "
-                       f"from a {rows * row_bytes / 1e9:.1f} GB np.memmap in {path_dir} (ids mod {rows})")
+                       f"from a {rows * row_bytes / 1e9:.1f} GB np.memmap in {path_dir}, page cache warm; "
+                       f"{mapping}")
+
+
+def cpu_mmap_gather_cold(cfg, ids, seconds_budget=15.0, file_gb=4.0):
+    """The same gather from a memmap whose pages are not in the OS page cache:
+    a file on the local disk, written, synced and dropped from the cache
+    (posix_fadvise DONTNEED) before a bounded sample of one minibatch's ids is
+    gathered in chunks. The reference's loader reads its feature file this way
+    when the file is larger than host RAM."""
+    import tempfile
+
+    from oracle import oracle
+
+    dim, dt = cfg["dim"], cfg["dtype"]
+    row_bytes = dim * ESIZE[dt]
+    d = tempfile.gettempdir()
+    try:
+        st = os.statvfs(d)
+        free = st.f_bavail * st.f_frsize
+    except OSError:
+        free = 0
+    rows = max(1, min(cfg["nodes"], int(min(file_gb * 1e9, 0.3 * free)) // row_bytes))
+    if rows * row_bytes < 1e9:
+        return {"note": f"no room for a cold-cache file in {d}"}
+    path = os.path.join(d, f"gids_b200_cold_{os.getpid()}.bin")
+    try:
+        mm = np.memmap(path, dtype=np.dtype(dt), mode="w+", shape=(rows, dim))
+        oracle.synth_fill_into(KIND[dt], 1, 0, mm.reshape(-1))
+        mm.flush()
+        del mm
+        fd = os.open(path, os.O_RDONLY)
+        try:
+            os.fsync(fd)
+            os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+        finally:
+            os.close(fd)
+        feat = oracle.open_memmap_table(path, np.dtype(dt), rows, dim)
+        ids_m = torch.as_tensor(_flat_ids(cfg, ids) % rows)
+        done, t_total = 0, 0.0
+        for lo in range(0, ids_m.numel(), 16384):
+            part = ids_m[lo:lo + 16384]
+            t0 = time.perf_counter()
+            out = oracle.mmap_index_select(feat, part)
+            t_total += time.perf_counter() - t0
+            done += out.shape[0]
+            del out
+            if t_total >= seconds_budget:
+                break
+        del feat
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    return {"value": round(done * row_bytes / 1e9 / t_total, 3), "unit": "GB/s", "rows": done,
+            "sample": f"first {done} ids of one minibatch gathered by torch.index_select from a "
+                      f"{rows * row_bytes / 1e9:.1f} GB np.memmap on the local disk ({d}) after fsync + "
+                      f"posix_fadvise(DONTNEED)"}
+
+
+# ------------------------------------------------------------------ parity
+def parity_check(cfg, ids, feat, hmap, n_rows: int, seed: int = 0) -> dict:
+    """Compares n_rows gathered rows per node type (a seeded random subset,
+    always with the first and the last row) bit for bit with the oracle's
+    restatement of the reference gather over the same synthetic table."""
+    from oracle import oracle
+
+    dim, dt = cfg["dim"], cfg["dtype"]
+    _, _, wrap = backing_geometry(cfg)
+    rng = np.random.default_rng(seed)
+    if isinstance(feat, dict):
+        items = [(k, ids[k], feat[k], hmap[k]) for k in feat]
+    else:
+        items = [(None, ids, feat, 0)]
+    checked, bad = 0, 0
+    for _, idv, out, key_off in items:
+        n = int(idv.numel())
+        if n == 0:
+            continue
+        m = min(n, n_rows)
+        pick = np.unique(np.concatenate([[0, n - 1], rng.choice(n, size=m, replace=False)]))
+        pt = torch.as_tensor(pick, device=out.device)
+        got = out.index_select(0, pt).cpu().numpy()
+        want = oracle.gather_synth(KIND[dt], 1, cfg["nodes"], dim, dim, idv.index_select(0, pt.to(idv.device)).cpu()
+                                   .numpy(), key_off=key_off, wrap_elems=wrap)
+        same = np.all(got.view(np.uint8).reshape(len(pick), -1) == want.view(np.uint8).reshape(len(pick), -1), axis=1)
+        bad += int((~same).sum())
+        checked += len(pick)
+    return {"rows_checked": checked, "ok": bad == 0, "mismatched_rows": bad}
 
 
 # ------------------------------------------------------------------ our arm
@@ -485,13 +594,20 @@ def run_ours(args, cfg, dist: Dist):
     g.window_buffering_flag = wbf
     t_cw = time.time() - t0
     log(f"[rank {dist.rank}] cache warm-up: {n_cw} minibatches in {t_cw:.1f}s")
+    last = None
     for i in range(args.warmup):
-        g.fetch_feature(dim, dev_it, device)
+        last = g.fetch_feature(dim, dev_it, device)  # held like the timed loop's last step
     torch.cuda.synchronize()
     bam.reset_stats()
 
     hbm_peak, hbm_src = measured_hbm_peak()
     host_peak = host_link_peak_gbs(device, dist)
+    nvlink_peak = None
+    if g.world > 1:
+        # every rank copies 1 GiB from the next rank's shard at the same time
+        dist.barrier()
+        nvlink_peak = bam.peer_copy_gbs((dist.rank + 1) % g.world, 1 << 30)
+        dist.barrier()
 
     # ---- timed region 1: node ids resident in HBM
     clocks = ClockSampler(dist.local)
@@ -503,7 +619,7 @@ def run_ours(args, cfg, dist: Dist):
     torch.cuda.nvtx.range_push("gids_timed_value")
     ev0.record(stream)
     for _ in dev_ids:
-        g.fetch_feature(dim, dev_it, device)
+        last = g.fetch_feature(dim, dev_it, device)
     ev1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -514,10 +630,12 @@ def run_ours(args, cfg, dist: Dist):
     k_ms = bam.kernel_time_ms()
     launches = st["launches"]
     rows_val = st["rows"]
+    # bit-exact spot check of the last timed minibatch (ids in HBM) against the oracle
+    parity = [parity_check(cfg, last[0], last[-1], hmap, args.parity_rows, seed=dist.rank)]
+    del last
 
     # ---- timed region 2: end to end through GIDS.fetch_feature, ids in pinned host memory
-    g.window_buffer.clear()  # a fresh iterator starts a fresh window
-    g.wb_init = False
+    g.drop_window_buffer()  # a fresh iterator starts a fresh window; the old one's marks are taken back
     first = args.warmup + args.steps + wb
     e2e_batches = host_batches[first:first + args.steps]
     it = ([b] for b in host_batches[first:])
@@ -533,13 +651,15 @@ def run_ours(args, cfg, dist: Dist):
     torch.cuda.nvtx.range_push("gids_timed_e2e")
     e0.record(stream)
     checks = 0.0
-    for _ in e2e_batches:
+    for i in range(len(e2e_batches)):
         batch = g.fetch_feature(dim, it, device)
         feat = batch[-1]
         if isinstance(feat, dict):
             feat = feat[max(feat, key=lambda k: feat[k].shape[0])]
         checks += float(feat[-1, -1].item())  # D2H read of the step's result
-        del batch, feat  # the step is done with its features, as a training step would be
+        del feat  # the step is done with its features, as a training step would be
+        if i + 1 < len(e2e_batches):
+            del batch
     e1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -548,6 +668,9 @@ def run_ours(args, cfg, dist: Dist):
     t_e2e = e0.elapsed_time(e1) / 1e3
     st_e2e = bam.get_stats()
     rows_e2e = st_e2e["rows"]
+    # and of the last end-to-end minibatch (ids from pinned host memory)
+    parity.append(parity_check(cfg, batch[0], batch[-1], hmap, args.parity_rows, seed=100 + dist.rank))
+    del batch
 
     # ---- loader: the sampler on a side stream overlapped with the gather, fresh
     #      minibatches (other sampler seeds); wall time with the device idle at both ends
@@ -555,8 +678,7 @@ def run_ours(args, cfg, dist: Dist):
     if not args.no_loader:
         side = torch.cuda.Stream(device)
         sample_ms = time_sampler(cfg, args.steps, dist.rank + 3571, device, side)
-        g.window_buffer.clear()
-        g.wb_init = False
+        g.drop_window_buffer()
         lit = SideStreamBatches(batch_stream(cfg, args.steps + wb, dist.rank + 3571, device), side, stream)
         if wb:
             g.fill_wb(lit, wb)
@@ -596,8 +718,8 @@ def run_ours(args, cfg, dist: Dist):
     alg_hbm = r_hbm_src + rows_l * row_bytes + 8 * rows_l  # source reads of hits + output writes + ids
     r_peer = st.get("bytes_peer", 0) / n_launch  # hit bytes read from other ranks' shards over NVLink
     terms = {"hbm": (alg_hbm, hbm_peak), "host_link": (r_host, host_peak)}
-    if dist.world > 1:
-        terms["nvlink"] = (r_peer, NVLINK_PEER_GBS)
+    if nvlink_peak:
+        terms["nvlink"] = (r_peer, nvlink_peak)
     bound = max(terms, key=lambda k: terms[k][0] / terms[k][1])
     t_star = terms[bound][0] / (terms[bound][1] * 1e9)
     achieved, peak, unit_peak = terms[bound][0] / t_launch / 1e9, terms[bound][1], "GB/s"
@@ -610,13 +732,15 @@ def run_ours(args, cfg, dist: Dist):
         "peak_source": {"hbm": hbm_src + " (of measured)",
                         "host_link": "pinned host->device copy measured live in this run, all ranks copying at "
                                      "once (of measured)",
-                        "nvlink": "peer copy per direction per GPU measured on this pool's B200s (of measured, "
-                                  "not live)"}[bound],
+                        "nvlink": "device-to-device copy of 1 GiB from the next rank's shard, all ranks copying "
+                                  "at once, measured live in this run (of measured)"}[bound],
         "model": "T* = max((R*(n_hit + n) + 8n)/BW_hbm, R*(n_cpu + n_miss + n_bypass)/BW_host, R*n_peer/BW_nvlink); "
                  "frac = T*/T_launch",
         "t_launch_ms": round(t_launch * 1e3, 3), "t_star_ms": round(t_star * 1e3, 3),
         "nvlink": {"alg_bytes_per_launch": int(r_peer), "achieved_gbs": round(r_peer / t_launch / 1e9, 1),
-                   "peak_gbs": NVLINK_PEER_GBS} if dist.world > 1 else None,
+                   "peak_gbs": round(nvlink_peak, 1),
+                   "peak_method": "cudaMemcpyAsync of 1 GiB from rank+1's shard, every rank at once, best of 3"}
+        if nvlink_peak else None,
         "hbm": {"alg_bytes_per_launch": int(alg_hbm), "achieved_gbs": round(alg_hbm / t_launch / 1e9, 1),
                 "peak_gbs": hbm_peak},
         "host_link": {"alg_bytes_per_launch": int(r_host), "achieved_gbs": round(r_host / t_launch / 1e9, 2),
@@ -636,26 +760,29 @@ def run_ours(args, cfg, dist: Dist):
         loader["gather_ms_per_minibatch"] = round(t_val_max / len(dev_ids) * 1e3, 2)
     e2e_value = rows_e2e_all * row_bytes / 1e9 / t_e2e_max
     result = {
-        "metric": "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs",
+        "metric": METRIC,
         "value": round(value, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t_val_max / len(dev_ids) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt],
-        "data": "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)",
+        "data": DATA,
         "minibatches_per_s": round(steps_all / t_val_max, 3),
-        "config": {"workload": workload_name(args, cfg),
-                   "global_batch": cfg["batch"] * dist.world,
-                   "parallelism": f"dp{dist.world} (independent trainers" +
-                                  (", page cache sharded by page id over NVLink)" if g.world > 1 else ")"),
-                   "backing_store": {"logical_bytes": range_bytes, "physical_bytes": geo["wrap_pages"] * page,
-                                     "wrap_pages": geo["wrap_pages"]},
-                   "l2": (f"no flush: every step reads {min(sizes) * row_bytes / 1e9:.2f} GB or more (L2 is 126 MB)"
-                          if min(sizes) * row_bytes > 126e6 else "steps smaller than L2: not a timing run"),
-                   "input_nodes_per_step": round(rows_val / max(1, len(dev_ids)), 1),
-                   "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
-                   "window_buffer_depth": wb,
-                   "cache_policy": args.policy,
-                   "cache_warmup_minibatches": n_cw,
-                   "gather_grid_cap": args.gather_blocks or None},
+        "config": workload_config(args, cfg, dist.world),
+        "settings": {"trainers": f"{dist.world} independent data-parallel trainers" +
+                                 (", page cache sharded by page id over NVLink" if g.world > 1 else ""),
+                     "wrap_pages": geo["wrap_pages"],
+                     "bytes_per_step_min": int(min(sizes) * row_bytes),
+                     "input_nodes_per_step": round(rows_val / max(1, len(dev_ids)), 1),
+                     "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
+                     "window_buffer_depth": wb,
+                     "cache_policy": args.policy,
+                     "cache_warmup_minibatches": n_cw,
+                     "gather_grid_cap": args.gather_blocks or None},
+        "parity": {"rows_checked": int(dist.sum(sum(p["rows_checked"] for p in parity))),
+                   "ok": bool(dist.sum(0.0 if all(p["ok"] for p in parity) else 1.0) == 0.0),
+                   "against": "oracle.gather_synth: the reference's gather restated over the same synthetic "
+                              "table (bit-exact)",
+                   "minibatches": "the last timed step (ids in HBM) and the last e2e step (ids from host), "
+                                  "every rank"},
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "api": "GIDS.fetch_feature",
                 "h2d_bytes_per_step": int(np.mean([nrows(b) * 8 for b in e2e_batches])),
@@ -673,6 +800,32 @@ def run_ours(args, cfg, dist: Dist):
     return result, batches
 
 
+def backing_geometry(cfg):
+    """(logical range bytes, bytes the emulated SSDs physically hold, wrap period
+    in elements or 0): the SSDs hold phys_gb of pages and logical page p is
+    stored where page p mod (their page count) is."""
+    esize, page = ESIZE[cfg["dtype"]], cfg["page"]
+    range_bytes = cfg["nodes"] * cfg["dim"] * esize
+    phys = min(int(cfg["phys_gb"] * 1e9), range_bytes)
+    if phys >= range_bytes:
+        return range_bytes, range_bytes, 0
+    per_ssd = (phys // cfg["ssds"]) // page * page
+    wrap_pages = per_ssd // page * cfg["ssds"]
+    return range_bytes, wrap_pages * page, wrap_pages * page // esize
+
+
+def workload_config(args, cfg, world: int) -> dict:
+    """The JSON line's `config`, identical in both arms: what is gathered, not how."""
+    logical, physical, _ = backing_geometry(cfg)
+    return {"workload": workload_name(args, cfg),
+            "global_batch": cfg["batch"] * world,
+            "parallelism": f"dp{world}",
+            "backing_store": {"logical_bytes": logical, "physical_bytes": physical},
+            "node_ids": "seeded synthetic graph + counter-hashed neighbour sampler: both arms gather the same "
+                        "minibatches",
+            "l2": "no flush: every step gathers millions of rows (GBs), far larger than the 126 MB L2"}
+
+
 def workload_name(args, cfg) -> str:
     """The workload as both arms name it in their JSON line."""
     dt, dim, page = cfg["dtype"], cfg["dim"], cfg["page"]
@@ -683,31 +836,37 @@ def workload_name(args, cfg) -> str:
 
 
 def run_reference(args, cfg, dist: Dist):
-    """The reference's CPU gather (the mmap baseline) on the host cores."""
+    """The reference's CPU implementation of the path -- the mmap baseline
+    gather -- on the host cores, over the same minibatches as our arm (the
+    sampler is drawn on the CPU; its counter-hashed choices make the node ids
+    identical to the GPU arm's). Nothing of the product is loaded: the
+    synthetic graph and sampler are plain torch, and the gather runs through
+    the oracle's restatement of the reference idiom."""
     if dist.rank != 0:
         return None
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
     n = args.warmup + args.steps
-    batches, _ = make_batches(cfg, n, 0, dev)
-    batches = [{k: v.cpu() for k, v in b.items()} if isinstance(b, dict) else b.cpu() for b in batches]
+    t0 = time.time()
+    batches, _ = make_batches(cfg, n, 0, "cpu")
+    t_sample = time.time() - t0
     dt, dim = cfg["dtype"], cfg["dim"]
-    row_bytes = dim * ESIZE[dt]
     # each step is one whole minibatch gathered by torch.index_select from the memmap
     res = cpu_mmap_gather(cfg, batches[args.warmup:], 1e9, file_gb=args.cpu_file_gb,
                           warmup_ids=batches[:args.warmup])
+    cold = cpu_mmap_gather_cold(cfg, batches[args.warmup]) if not args.no_cold else None
     v = res["value"]
     return {
-        "impl": "reference", "metric": "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs",
+        "impl": "reference", "metric": METRIC,
         "value": round(v, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(res["seconds"] / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt], "data": "synthetic",
+        "vs_baseline": None, "dtype": {"float32": "f32", "float16": "f16"}[dt], "data": DATA,
         "minibatches_per_s": round(res["minibatches_per_s"], 3),
-        "config": {"workload": workload_name(args, cfg), "global_batch": cfg["batch"],
-                   "parallelism": "host cores (rank 0 only)"},
+        "config": workload_config(args, cfg, dist.world),
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": res["cores"], "kind": "port",
                          "sample": res["sample"],
-                         **{k: res[k] for k in ("h2d_gbs", "with_h2d_gbs", "h2d_note") if k in res}},
+                         **{k: res[k] for k in ("h2d_gbs", "with_h2d_gbs", "h2d_note") if k in res},
+                         "cold_page_cache": cold},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": {"sampling_cpu": round(t_sample, 1), "memmap_fill": res["fill_s"]},
     }
 
 
@@ -719,7 +878,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--phys-gb", type=float, default=0.0, help="GB of pages the emulated SSDs hold (0: the config's)")
-    ap.add_argument("--cpu-file-gb", type=float, default=8.0, help="size of the CPU-baseline memmap")
+    ap.add_argument("--cpu-file-gb", type=float, default=0.0,
+                    help="size of the CPU-baseline memmap (0: the bytes the emulated SSDs hold, <= 40%% of RAM)")
+    ap.add_argument("--no-cold", action="store_true", help="reference arm: skip the cold-page-cache sample")
+    ap.add_argument("--parity-rows", type=int, default=4096,
+                    help="gathered rows per checked minibatch compared bit for bit with the oracle")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--nodes", type=int, default=0, help="override the node count (small profiling cases)")
     ap.add_argument("--cache-mb", type=int, default=0, help="override the cache size")
@@ -763,6 +926,7 @@ def main():
         return
 
     dist.init("nccl", torch.device("cuda", dist.local))
+    exit_code = 0
     try:
         res, batches = run_ours(args, cfg, dist)
         if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
@@ -770,6 +934,9 @@ def main():
         if dist.rank == 0:
             print(json.dumps(res), flush=True)
         dist.barrier()
+        if not res["parity"]["ok"]:
+            log(f"[rank {dist.rank}] PARITY FAILURE: gathered rows differ from the oracle: {res['parity']}")
+            exit_code = 1
     finally:
         if (dist.world > 1 or args.shared_backing) and dist.rank == 0:  # the shared emulated SSD files
             import glob
@@ -777,6 +944,8 @@ def main():
             for f in glob.glob(f"/dev/shm/gids_b200_bench_{os.environ.get('MASTER_PORT', 'x')}_ssd*"):
                 os.unlink(f)
         dist.close()
+    if exit_code:
+        sys.exit(exit_code)
 
 
 if __name__ == "__main__":

@@ -28,14 +28,22 @@ from collections.abc import Mapping
 
 import torch
 
-import BAM_Feature_Store
-
+# feature element type -> BAM_Feature_Store class name
 _STORE_CLASSES = {
-    torch.float32: BAM_Feature_Store.BAM_Feature_Store_float,
-    torch.int64: BAM_Feature_Store.BAM_Feature_Store_long,
-    torch.float16: BAM_Feature_Store.BAM_Feature_Store_half,
-    torch.bfloat16: BAM_Feature_Store.BAM_Feature_Store_bfloat16,
+    torch.float32: "BAM_Feature_Store_float",
+    torch.int64: "BAM_Feature_Store_long",
+    torch.float16: "BAM_Feature_Store_half",
+    torch.bfloat16: "BAM_Feature_Store_bfloat16",
 }
+
+
+def _feature_store_module():
+    """The compiled BAM_Feature_Store module, imported on first use so that
+    importing this package maps no library (ImportError if it is not built:
+    there is no CPU fallback)."""
+    import BAM_Feature_Store
+
+    return BAM_Feature_Store
 
 
 def _current_stream_handle(device: torch.device) -> int:
@@ -91,7 +99,8 @@ class GIDS:
         if dtype not in _STORE_CLASSES:
             raise ValueError(f"unsupported feature dtype {dtype}")
         self.dtype = dtype
-        self.BAM_FS = _STORE_CLASSES[dtype]()
+        BAM_Feature_Store = _feature_store_module()
+        self.BAM_FS = getattr(BAM_Feature_Store, _STORE_CLASSES[dtype])()
 
         self.accumulator_flag = accumulator_flag
         self.required_accesses = 0
@@ -226,6 +235,31 @@ class GIDS:
             batch = next(it)
             self.window_buffer.append(batch)
             self.window_buffering(batch)
+
+    def drop_window_buffer(self):
+        """Abandon the queued window (extension): the marks of every batch still
+        in it are taken back, so its pages no longer resist eviction, and the
+        next ``fetch_feature`` refills the window from its own iterator. The
+        reference has no counterpart; its marks of an abandoned window stay."""
+        if self.window_buffering_flag:
+            stream = _current_stream_handle(self.device)
+            # the accumulator has already gathered (and unpinned) the first
+            # len(return_torch_buffer) batches of the window
+            for batch in self.window_buffer[len(self.return_torch_buffer):]:
+                for key, value in self._batch_ids(batch):
+                    if len(value) == 0:
+                        continue
+                    t = _as_index(value, self.device)
+                    self.BAM_FS.unset_window_buffering(t.data_ptr(), len(t), key, stream)
+        self.window_buffer.clear()
+        self.return_torch_buffer.clear()
+        self.wb_init = False
+
+    def _batch_ids(self, batch):
+        """(key offset, ids) of every node type of a batch."""
+        if self.heterograph:
+            return [(self._key_off(k), v) for k, v in batch[0].items()]
+        return [(0, batch[0])]
 
     # ----------------------------------------------- storage access accumulator
     def set_required_storage_access(self, bw, l_ssd, l_system, num_ssd, p):

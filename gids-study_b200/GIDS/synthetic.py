@@ -18,6 +18,12 @@ hop h (from the seeds outward) takes min(f_{L-1-h}, in_degree) distinct
 in-edges of every node of the current frontier; the next frontier is the
 current node set plus the new sources in order of first appearance, and the
 last node set is ``input_nodes`` (seeds first).
+
+Every random choice is a pure function of integers (counter-based SplitMix64
+hashes), not of a random generator's stream, so a minibatch is the same on
+the CPU, on any GPU and in the CUDA sampler kernel of this package: the
+in-edges a node keeps at a hop are the ones with the smallest
+``edge_key(hop_seed(seed, call, hop), v, j)``, listed in increasing key order.
 """
 from __future__ import annotations
 
@@ -50,6 +56,34 @@ def _mix(z: torch.Tensor) -> torch.Tensor:
 def _uniform(z: torch.Tensor) -> torch.Tensor:
     """uniform [0, 1) float64 from 53 hash bits"""
     return _srl(_mix(z), 11).to(torch.float64) * (2.0 ** -53)
+
+
+_MASK64 = (1 << 64) - 1
+EDGE_INDEX_BITS = 24  # an edge key keeps j in its low bits: in-degrees below 2^24
+
+
+def mix64(x: int) -> int:
+    """SplitMix64 finalizer (Steele, Lea, Flood 2014) on a Python int."""
+    x &= _MASK64
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & _MASK64
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & _MASK64
+    return x ^ (x >> 31)
+
+
+def hop_seed(seed: int, call: int, hop: int) -> int:
+    """Key seed (a signed 64-bit value) of hop ``hop`` of the ``call``-th
+    minibatch a sampler of seed ``seed`` draws."""
+    return _i64(mix64(seed * 0x9E3779B97F4A7C15 + call * 0xD1B54A32D192ED03 + hop * 0x8CB92BA72F3D8DD7 +
+                      0x632BE59BD9B4E019))
+
+
+def edge_key(seed_h: int, v: torch.Tensor, j: torch.Tensor) -> torch.Tensor:
+    """Selection key of in-edge j of node v at a hop of seed ``seed_h``: 39
+    hash bits above the edge index j (24 bits), so the keys of one node are
+    distinct and nonnegative, and sorting them needs no tie rule."""
+    z = _mix(v * int(_G) + int(seed_h))
+    z = _mix(z + (j + 1) * int(_M2))
+    return (_srl(z, 1 + EDGE_INDEX_BITS) << EDGE_INDEX_BITS) | j
 
 
 def zipf_truncation(alpha: float, mean: float) -> int:
@@ -148,29 +182,37 @@ def unique_first(x: torch.Tensor) -> torch.Tensor:
 
 
 class NeighborSampler:
-    """Seeded stand-in for dgl.dataloading.MultiLayerNeighborSampler(fanouts)."""
+    """Seeded stand-in for dgl.dataloading.MultiLayerNeighborSampler(fanouts).
+
+    The ``call``-th ``sample`` draws hop ``h`` with key seed
+    ``hop_seed(seed, call, h)``; each node of the frontier keeps its
+    min(fanout, in_degree) in-edges of smallest ``edge_key``."""
 
     def __init__(self, graph: SyntheticGraph, fanouts, seed: int = 1000):
         self.g = graph
         self.fanouts = [int(f) for f in fanouts]
-        self.gen = torch.Generator(device=graph.device)
-        self.gen.manual_seed(int(seed))
+        self.seed = int(seed)
+        self.calls = 0
 
-    def sample_neighbors(self, frontier: torch.Tensor, fanout: int):
-        """(dst, src) pairs: min(fanout, deg) distinct in-edges per frontier node."""
+    def sample_neighbors(self, frontier: torch.Tensor, fanout: int, seed_h: int):
+        """(dst, src) pairs: the min(fanout, deg) in-edges of smallest key per
+        frontier node, dst-major, keys increasing."""
         g = self.g
-        deg = g.in_degree(frontier)
         if frontier.numel() == 0:
             return frontier, frontier
+        deg = g.in_degree(frontier)
         D = int(deg.max().item())
         if D == 0:
             e = frontier[:0]
             return e, e
-        keys = torch.rand((frontier.numel(), D), generator=self.gen, device=frontier.device)
+        if D >= (1 << EDGE_INDEX_BITS):
+            raise ValueError("in-degree too large for the edge key")
         pos = torch.arange(D, device=frontier.device)
-        keys.masked_fill_(pos[None, :] >= deg[:, None], 2.0)
+        keys = edge_key(seed_h, frontier[:, None], pos[None, :])
+        keys.masked_fill_(pos[None, :] >= deg[:, None], torch.iinfo(torch.int64).max)
         take = min(fanout, D)
-        j = torch.topk(keys, take, dim=1, largest=False).indices
+        # keys are distinct within a row: the k smallest, in order, are well defined
+        j = torch.topk(keys, take, dim=1, largest=False, sorted=True).indices
         valid = torch.arange(take, device=frontier.device)[None, :] < torch.clamp(deg, max=fanout)[:, None]
         dst = frontier[:, None].expand(-1, take)[valid]
         jj = j[valid]
@@ -178,9 +220,11 @@ class NeighborSampler:
 
     def sample(self, seeds: torch.Tensor):
         """input_nodes (seeds first, then new sources by first appearance), seeds."""
+        call = self.calls
+        self.calls += 1
         nodes = unique_first(seeds.to(self.g.device))
-        for f in reversed(self.fanouts):
-            _, src = self.sample_neighbors(nodes, f)
+        for hop, f in enumerate(reversed(self.fanouts)):
+            _, src = self.sample_neighbors(nodes, f, hop_seed(self.seed, call, hop))
             new = unique_first(src)
             new = new[~torch.isin(new, nodes)]
             nodes = torch.cat([nodes, new])
@@ -189,15 +233,20 @@ class NeighborSampler:
 
 def seed_batches(num_nodes: int, batch_size: int, n_batches: int, seed: int, device="cpu", zipf_alpha=None):
     """Batches of distinct seed nodes: uniform over [0, N) or, with zipf_alpha,
-    Zipf over node ids (ranks scattered over the id space by a hash)."""
-    gen = torch.Generator(device=device)
-    gen.manual_seed(int(seed))
+    Zipf over node ids (ranks scattered over the id space by a hash). Drawn
+    on the CPU from a counter-based hash of (seed, draw index), so the batches
+    do not depend on the device they are moved to."""
     a = None if zipf_alpha is None else float(zipf_alpha)
+    base = _i64(mix64(int(seed) * 0xA0761D6478BD642F + 0xE7037ED1A0B428DB))
+    counter = [0]
 
     def draw(m):
+        k = torch.arange(counter[0], counter[0] + m, dtype=torch.int64)
+        counter[0] += m
+        z = _mix(k * int(_G) + base)
         if a is None:
-            return torch.randint(0, num_nodes, (m,), generator=gen, device=device)
-        u = torch.rand(m, generator=gen, device=device, dtype=torch.float64)
+            return _srl(z, 1) % num_nodes
+        u = _srl(z, 11).to(torch.float64) * (2.0 ** -53)
         if abs(a - 1.0) < 1e-9:
             r = torch.exp(u * math.log(num_nodes))
         else:
@@ -214,7 +263,7 @@ def seed_batches(num_nodes: int, batch_size: int, n_batches: int, seed: int, dev
                 break
             more = draw(batch_size * 4)
             s = unique_first(torch.cat([s, more]))
-        out.append(s[:batch_size])
+        out.append(s[:batch_size].to(device))
     return out
 
 
@@ -291,19 +340,22 @@ class HeteroNeighborSampler:
         self.g = graph
         self.fanouts = [int(f) for f in fanouts]
         self.samplers = {r: NeighborSampler(g, [1], seed=seed + 7 * i) for i, (r, g) in enumerate(graph.rel.items())}
+        self.calls = 0
 
     def sample(self, seeds: dict):
         """{type: input node ids (type-local ids, seeds first)}, seeds."""
         dev = self.g.device
+        call = self.calls
+        self.calls += 1
         nodes = {t: torch.zeros(0, dtype=torch.int64, device=dev) for t in self.g.type_sizes}
         for t, s in seeds.items():
             nodes[t] = unique_first(s.to(dev))
-        for f in reversed(self.fanouts):
+        for hop, f in enumerate(reversed(self.fanouts)):
             new = {t: [] for t in nodes}
             for (src, dst), smp in self.samplers.items():
                 if nodes[dst].numel() == 0:
                     continue
-                _, nb = smp.sample_neighbors(nodes[dst], f)
+                _, nb = smp.sample_neighbors(nodes[dst], f, hop_seed(smp.seed, call, hop))
                 new[src].append(nb)
             for t, parts in new.items():
                 if not parts:

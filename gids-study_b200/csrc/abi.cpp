@@ -271,6 +271,15 @@ int gids_store_share_shards(gids_store_t* const* stores, int n) {
   });
 }
 
+int gids_store_peer_copy_gbs(gids_store_t* s, int peer, uint64_t bytes, double* out) {
+  return guarded([&] {
+    NEED(s);
+    NEED(out);
+    GIDS_CHECK(peer >= 0, GIDS_E_INVAL, "peer must be >= 0");
+    *out = s->s.peer_copy_gbs((uint32_t)peer, bytes);
+  });
+}
+
 int gids_read_feature(gids_store_t* s, void* out, const int64_t* idx, int64_t n, int dim, int cache_dim,
                       uint64_t key_off, void* stream) {
   return guarded([&] {
@@ -303,6 +312,14 @@ int gids_set_window_buffering(gids_store_t* s, const int64_t* idx, int64_t n, in
   return guarded([&] {
     NEED(s);
     s->s.window_buffering(idx, n, hash_off, row_stride_elems, (cudaStream_t)stream);
+  });
+}
+
+int gids_unset_window_buffering(gids_store_t* s, const int64_t* idx, int64_t n, int64_t hash_off,
+                                uint32_t row_stride_elems, void* stream) {
+  return guarded([&] {
+    NEED(s);
+    s->s.window_buffering(idx, n, hash_off, row_stride_elems, (cudaStream_t)stream, true);
   });
 }
 

@@ -128,6 +128,10 @@ class FeatureStore {
   void set_window_buffering(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
     check(gids_set_window_buffering(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
   }
+  // extension: take back the marks of a window that will not be gathered
+  void unset_window_buffering(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
+    check(gids_unset_window_buffering(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
+  }
   // cpu_backing_buffer (gids_nvme.cu:123-139)
   void cpu_backing_buffer(uint64_t dim, uint64_t len) { check(gids_cpu_backing_buffer(s(), dim, len)); }
   // set_cpu_buffer (gids_nvme.cu:694-711)
@@ -190,6 +194,12 @@ class FeatureStore {
   void set_cache_policy(bool admission, uint32_t ref_max) { check(gids_store_set_cache_policy(s(), admission ? 1 : 0, ref_max)); }
   // cap on the gather's grid (0: every resident block)
   void set_gather_blocks(uint32_t n) { check(gids_store_set_gather_blocks(s(), n)); }
+  // NVLink bandwidth: a timed copy from a peer rank's shard (GB/s)
+  double peer_copy_gbs(int peer, uint64_t bytes) {
+    double v = 0.0;
+    check(gids_store_peer_copy_gbs(s(), peer, bytes, &v));
+    return v;
+  }
   py::bytes ipc_handle() {
     char h[64];
     check(gids_store_ipc_handle(s(), h, sizeof(h)));
@@ -291,6 +301,8 @@ void bind_store(py::module_& m, const char* name) {
            py::arg("stream") = 0, R())
       .def("set_window_buffering", &S::set_window_buffering, py::arg("id_idx"), py::arg("num_pages"),
            py::arg("hash_off") = 0, py::arg("stream") = 0, R())
+      .def("unset_window_buffering", &S::unset_window_buffering, py::arg("id_idx"), py::arg("num_pages"),
+           py::arg("hash_off") = 0, py::arg("stream") = 0, R())
       .def("cpu_backing_buffer", &S::cpu_backing_buffer, py::arg("dim"), py::arg("len"), R())
       .def("set_cpu_buffer", &S::set_cpu_buffer, py::arg("idx_buffer"), py::arg("num"), R())
       .def("flush_cache", &S::flush_cache, R())
@@ -314,6 +326,7 @@ void bind_store(py::module_& m, const char* name) {
       .def("set_cache_policy", &S::set_cache_policy, py::arg("admission"), py::arg("ref_max"))
       .def("set_gather_blocks", &S::set_gather_blocks, py::arg("max_blocks"))
       .def("ipc_handle", &S::ipc_handle)
+      .def("peer_copy_gbs", &S::peer_copy_gbs, py::arg("peer"), py::arg("bytes"), R())
       .def("open_peers", &S::open_peers)
       .def("set_synchronous", &S::set_synchronous, R())
       .def("set_row_layout", &S::set_row_layout, R())

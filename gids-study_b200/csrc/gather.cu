@@ -276,6 +276,7 @@ struct TmaPipe {
   uint32_t op, oc;
   uint32_t sb[TMA_STAGES];
   uint32_t phase;  // parity of each stage's next completion
+  uint32_t pend;   // stages whose loads were given up on and have not completed since
   int live;        // cleared for good if a stage ever fails to complete
 
   __device__ __forceinline__ bool pack(int s) {
@@ -321,6 +322,28 @@ struct TmaPipe {
     // the acquire on their page-table words); order them before the bulk reads
     asm volatile("fence.proxy.async.global;" ::: "memory");
     for (int s = 0; s < TMA_STAGES && pack(s); s++) issued++;
+  }
+  // Waits (bounded) for the bulk loads of every stage that was issued but
+  // not completed; true when none is left in flight. After a stage wait gave
+  // up, this decides whether the ring's shared memory and the slots the loads
+  // read can be let go (see the give-up path in the kernel).
+  __device__ __forceinline__ bool quiesce() {
+    // at most TMA_STAGES stages are in flight, each on its own mbarrier; the
+    // ones still outstanding are kept in `pend` across calls
+    if (done < issued) {
+      for (int k = done; k < issued; k++) pend |= 1u << (k % TMA_STAGES);
+      done = issued;
+    }
+    for (int s = 0; s < TMA_STAGES; s++) {
+      if (!((pend >> s) & 1u)) continue;
+      bool ok = false;
+      for (int rep = 0; rep < 4 && !ok; rep++) ok = mbar_wait(bar + s, (phase >> s) & 1u);
+      if (ok) {
+        phase ^= 1u << s;
+        pend &= ~(1u << s);
+      }
+    }
+    return pend == 0;
   }
   // false: a stage did not complete within the limit (the caller copies the
   // segments again another way)
@@ -402,11 +425,14 @@ __device__ __forceinline__ const char* backing_addr(const DevBacking& b, uint64_
   return b.ssd[c] + (dp << b.page_shift) + ((l & ((1ull << b.lpp_shift) - 1ull)) << line_shift);
 }
 
-// Saturating decrement of a window-buffer pin counter (bounded CAS loop).
+// Saturating decrement of a window-buffer pin counter. The CAS loop runs until
+// it lands or the counter reads 0: every failed CAS means another thread
+// changed the counter, so the loop is bounded by the contention on this one
+// word, and no pin is left behind when it is contended.
 template <bool SYS>
 __device__ __forceinline__ void wb_consume(unsigned int* w, unsigned int cnt) {
   unsigned int v = ld_relaxed_u32<SYS>(w);
-  for (int it = 0; v != 0 && it < 64; it++) {
+  while (v != 0) {
     const unsigned int nv = v > cnt ? v - cnt : 0u;
     const unsigned int r = atom_cas_u32<SYS>(w, v, nv);
     if (r == v) break;
@@ -467,6 +493,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     for (int s = 0; s < TMA_STAGES; s++) mbar_init(&tma_bar[wib][s]);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     pipe.phase = 0;
+    pipe.pend = 0;
     pipe.live = 1;
   }
   __syncwarp();
@@ -816,18 +843,32 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     if (VEC == 16 && nt && lane == 0)
       pipe.issue(sd + (32 - nt), nt, tma_ring_sh + (size_t)wib * TMA_STAGES * TMA_STAGE_BYTES, tma_bar[wib]);
     copy_segments<VEC>(sd, __popc(has), lane);  // overlaps the bulk loads in flight
+    bool keep_refs = false;
     if (VEC == 16 && nt) {
       bool ok = true;
       if (lane == 0) ok = pipe.drain();
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
-        // a bulk load did not complete: record it, stop using the ring, and copy
-        // this chunk's slot segments through registers (rewriting any bytes
-        // the pipeline already stored with the same values)
+        // A bulk load did not complete within the wait limit. The warp records
+        // it (GIDS_E_CUDA at the host), stops using the ring for good, and copies
+        // this chunk's slot segments through registers (rewriting any bytes the
+        // pipeline already stored with the same values). Loads still in flight
+        // write only into the ring, which nothing reads any more, and read only
+        // slots this chunk holds references on. Invariant: those references
+        // are dropped only once every load of the ring has completed
+        // (quiesce); if the loads are still outstanding after a second bounded
+        // wait, the chunk keeps its references (the lines stay resident until
+        // flush_cache) so no slot a load still reads can be evicted and
+        // refilled. Kernel exit waits for them once more (below); a load that
+        // never completes at all is the one case left undefined (the CTA exits
+        // with it in flight), and it is reported.
+        int q = 1;
         if (lane == 0) {
           pipe.live = 0;
           *reinterpret_cast<volatile int*>(a.host_err) = 2;
+          q = pipe.quiesce();
         }
+        keep_refs = __shfl_sync(0xffffffffu, q, 0) == 0;
         copy_segments<VEC>(sd + (32 - nt), nt, lane);
       }
     }
@@ -835,7 +876,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 
     GIDS_PHASE_MARK(tph3);
     // ---- release, clock reference bit, window-buffer consumption
-    if (took_ref) {
+    if (took_ref && !keep_refs) {
       red_add_release<SYS>(stw, (unsigned long long)(-(long long)cnt));
       if (gcls != CLS_BYPASS) {  // one more chance, up to the ceiling
         const unsigned char rr = S.slot_ref[gslot];
@@ -893,7 +934,11 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 
   __syncwarp();
   if (lane == 0) {
-    if (VEC == 16) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // the output's bulk stores
+    if (VEC == 16) {
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // the output's bulk stores
+      // loads given up on earlier: one more bounded wait before the CTA exits
+      if (pipe.pend && !pipe.quiesce()) *reinterpret_cast<volatile int*>(a.host_err) = 2;
+    }
 #pragma unroll
     for (int i = 0; i < K_N; i++)
       if (acc[i]) atomicAdd(a.stats + kStatMap[i], acc[i]);
@@ -902,7 +947,8 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 
 // Window buffering: one thread per node id, +1 on the pin counter of every
 // page its row touches, in the shard that owns the page (gids_kernel.cu:246-256
-// marks one page per id).
+// marks one page per id). With a.release, -1 instead (saturating at 0): the
+// marks of a window that will not be gathered are taken back.
 __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.n) return;
@@ -912,10 +958,18 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   const uint64_t b0 = (uint64_t)rs * a.stride;
   const uint64_t p0 = b0 >> a.page_shift, p1 = (b0 + a.row_bytes - 1) >> a.page_shift;
   for (uint64_t p = p0; p <= p1; p++) {
-    if (a.world == 1)
-      atomicAdd(a.wb[0] + p, 1u);
-    else
-      atomicAdd_system(a.wb[p % a.world] + p / a.world, 1u);
+    if (a.world == 1) {
+      if (a.release)
+        wb_consume<false>(a.wb[0] + p, 1u);
+      else
+        atomicAdd(a.wb[0] + p, 1u);
+    } else {
+      unsigned int* const w = a.wb[p % a.world] + p / a.world;
+      if (a.release)
+        wb_consume<true>(w, 1u);
+      else
+        atomicAdd_system(w, 1u);
+    }
   }
 }
 

@@ -153,6 +153,7 @@ struct WbArgs {
   uint64_t row_bytes;
   uint64_t n_rows;
   uint32_t page_shift;
+  uint32_t release;  // 0: add one pin per (row, page); 1: take one back (saturating)
 };
 
 // Launchers (gather.cu). sys = the cache is shared with other GPUs, so
@@ -224,7 +225,11 @@ class Store {
                         uint64_t num_ele, uint64_t num_ssd);
   void read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
                   int cache_dim, const uint64_t* key_offs, cudaStream_t st);
-  void window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st);
+  // release = false: mark the rows' lines (one pin per row and line);
+  // release = true: take those marks back (a window that will not be gathered)
+  void window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st,
+                        bool release = false);
+  void clear_window_pins();
   void cpu_backing_buffer(uint64_t dim, uint64_t len);
   void set_cpu_buffer(const int64_t* host_idx, int64_t num);
   void set_row_layout(uint32_t cache_dim);
@@ -273,6 +278,9 @@ class Store {
   void ipc_handle(void* out64);
   void open_peers(const void* handles, uint32_t n);
   static void share_in_process(Store* const* stores, uint32_t n);
+  // bandwidth of a device-to-device copy of `bytes` from rank `peer`'s shard
+  // into this GPU (GB/s, best of three): the link term of the roofline
+  double peer_copy_gbs(uint32_t peer, uint64_t bytes);
 
   // device allocations (this rank's shard lives in one allocation, d_shard)
   char* d_shard = nullptr;

@@ -11,11 +11,17 @@
 // neither reads nor writes.
 //
 // Properties a caller relies on:
-//  * the array is kNoallocScratchBytes (32 MiB) on every GPU that loads this
-//    library, held until the process exits;
-//  * the first call on a device looks the array's device address up
-//    (cudaGetSymbolAddress, with that device current) and keeps it; make that
-//    first call before any stream capture;
+//  * the array is kNoallocScratchBytes (32 MiB) on every GPU where it has
+//    been loaded, held until the process exits. CUDA loads a module's device
+//    arrays lazily, so the first call on a device is the one that makes the
+//    32 MiB resident (the driver reserves it while loading the module): make
+//    that first call early -- before another allocator reserves the rest of
+//    the device -- and before any stream capture. It also looks the array's
+//    device address up (cudaGetSymbolAddress, with that device current) and
+//    keeps it. Later calls allocate nothing;
+//  * its counters (rows, hits, misses, CPU-buffer rows, ...) are added to the
+//    store's statistics after each call by one small stream-ordered kernel,
+//    so gids_get_stats and gids_get_cpu_access_count include its rows;
 //  * every call starts from an empty cache: it clears the counters, the clock
 //    and the page table of the store's range on its stream before the launch,
 //    so a page fetched by several rows of one call crosses the host link once,
@@ -58,6 +64,13 @@ char* scratch_address(int device) {
 }
 
 uint64_t up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+// Adds the per-call counters kept in the scratch to the store's counters.
+__global__ void add_counters_kernel(unsigned long long* __restrict__ dst, const unsigned long long* __restrict__ src,
+                                    int n) {
+  const int i = threadIdx.x;
+  if (i < n && src[i]) atomicAdd(dst + i, src[i]);
+}
 
 }  // namespace
 
@@ -160,6 +173,12 @@ void Store::read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int 
   const uint64_t want_blocks = (a.total_chunks + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
   const int grid = (int)std::min<uint64_t>(want_blocks, (uint64_t)grid_blocks[0][vi]);
   launch_gather(a, vec, false, grid, st);
+  static_assert(GIDS_STAT_COUNT <= 32, "one warp adds the counters");
+  add_counters_kernel<<<1, 32, 0, st>>>(d_stats, a.stats, GIDS_STAT_COUNT);
+  GIDS_CUDA(cudaGetLastError());
+  launches++;
+  total_access += (uint64_t)n;
+  last_stream = st;
   if (synchronous) {
     GIDS_CUDA(cudaStreamSynchronize(st));
     check_async_error();

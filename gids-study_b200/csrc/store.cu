@@ -468,9 +468,10 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
   }
 }
 
-void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st) {
+void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st,
+                             bool release) {
   std::lock_guard<std::mutex> lk(mu);
-  NvtxRange nv("gids.window_buffering");
+  NvtxRange nv(release ? "gids.window_unmark" : "gids.window_buffering");
   GIDS_CHECK(initialized, GIDS_E_STATE, "set_window_buffering before init_controllers");
   GIDS_CHECK(n >= 0, GIDS_E_INVAL, "n must be >= 0");
   if (n == 0) return;
@@ -478,6 +479,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   DeviceGuard g(device);
   if (!d_wb) {
+    if (release) return;  // nothing was ever marked
     GIDS_CUDA(cudaMalloc(&d_wb, n_lines * sizeof(unsigned int)));
     GIDS_CUDA(cudaMemset(d_wb, 0, n_lines * sizeof(unsigned int)));
   }
@@ -494,6 +496,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   w.row_bytes = w.stride;
   w.n_rows = range_bytes >= w.row_bytes ? (range_bytes - w.row_bytes) / w.stride + 1 : 0;
   w.page_shift = line_shift;
+  w.release = release ? 1u : 0u;
   launch_wb_mark(w, st);
   last_stream = st;
   if (synchronous) GIDS_CUDA(cudaStreamSynchronize(st));
@@ -623,14 +626,23 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
   }
+  clear_window_pins();
   if (cpu_mode && cpu_filled_stride) fill_cpu_buffer(cpu_filled_stride);
   GIDS_CUDA(cudaDeviceSynchronize());
 }
 
+// Drops every window-buffer pin of this rank's shard (the whole range when
+// unsharded). A marked window that is never gathered would otherwise keep
+// its lines from being evicted for good.
+void Store::clear_window_pins() {
+  if (d_wb) GIDS_CUDA(cudaMemset(d_wb, 0, (world == 1 ? n_lines : n_lines_local) * sizeof(unsigned int)));
+}
+
 void Store::flush_cache() {
   // The cache never holds dirty pages (writes go straight to the backing
-  // store), so flushing only has to drop every resident page. A sharded
-  // cache drops this rank's shard: all ranks flush, with no gather in flight.
+  // store), so flushing only has to drop every resident page, and with them
+  // every window-buffer pin. A sharded cache drops this rank's shard: all
+  // ranks flush, with no gather in flight.
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(initialized, GIDS_E_STATE, "flush_cache before init_controllers");
   DeviceGuard g(device);
@@ -645,8 +657,51 @@ void Store::flush_cache() {
   const ShardLayout L(n_lines_local, n_slots, line_size, world > 1);
   GIDS_CUDA(cudaMemset(d_shard + L.seen, 0, L.seen_bytes));
   GIDS_CUDA(cudaMemset(d_shard + L.clock, 0, 8));
+  clear_window_pins();
   refs_since_seen_reset = 0;
   GIDS_CUDA(cudaDeviceSynchronize());
+}
+
+double Store::peer_copy_gbs(uint32_t peer, uint64_t bytes) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized && world > 1 && shards_ready, GIDS_E_STATE, "needs an attached sharded cache");
+  GIDS_CHECK(peer < world && peer != rank, GIDS_E_INVAL, "peer must be another rank of the cache");
+  const uint64_t have = shard_bytes & ~4095ull;
+  bytes = std::min<uint64_t>(bytes & ~4095ull, have);
+  GIDS_CHECK(bytes > 0, GIDS_E_INVAL, "nothing to copy");
+  DeviceGuard g(device);
+  // the peer's whole shard allocation: its base is the peer's page table
+  const char* src = reinterpret_cast<const char*>(shards[peer].state);
+  char* dst = nullptr;
+  cudaStream_t st = nullptr;
+  cudaEvent_t a = nullptr, b = nullptr;
+  double best = 0.0;
+  GIDS_CUDA(cudaMalloc(&dst, bytes));
+  try {
+    GIDS_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    GIDS_CUDA(cudaEventCreate(&a));
+    GIDS_CUDA(cudaEventCreate(&b));
+    for (int rep = 0; rep < 4; rep++) {  // the first is a warm-up
+      GIDS_CUDA(cudaEventRecord(a, st));
+      GIDS_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st));
+      GIDS_CUDA(cudaEventRecord(b, st));
+      GIDS_CUDA(cudaEventSynchronize(b));
+      float ms = 0.f;
+      GIDS_CUDA(cudaEventElapsedTime(&ms, a, b));
+      if (rep && ms > 0.f) best = std::max(best, (double)bytes / 1e9 / (ms / 1e3));
+    }
+  } catch (...) {
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dst);
+    throw;
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  cudaStreamDestroy(st);
+  cudaFree(dst);
+  return best;
 }
 
 void Store::synchronize() {

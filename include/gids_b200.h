@@ -166,6 +166,12 @@ GIDS_API int gids_store_set_sharding(gids_store_t *s, int world, int rank);
 GIDS_API int gids_store_ipc_handle(gids_store_t *s, void *out, size_t len);
 GIDS_API int gids_store_open_peers(gids_store_t *s, const void *handles, int world);
 GIDS_API int gids_store_share_shards(gids_store_t *const *stores, int n);
+/* Link bandwidth of an attached sharded cache (no reference counterpart; a
+ * measurement aid): copies `bytes` (rounded down to 4 KB, at most one shard)
+ * from rank `peer`'s shard into this GPU with cudaMemcpyAsync and returns the
+ * best of three timed copies in GB/s. Run it on every rank at once for the
+ * bandwidth a rank gets while the others also use their links. */
+GIDS_API int gids_store_peer_copy_gbs(gids_store_t *s, int peer, uint64_t bytes, double *out);
 
 /* -------------------------------------------------------------- gathers --
  * gids_read_feature replaces BAM_Feature_Store<T>::read_feature
@@ -192,15 +198,19 @@ GIDS_API int gids_read_feature_multi(gids_store_t *s, int k, void *const *outs, 
  * runtime, or a framework caching allocator that reserved the GPU), where a
  * cudaMalloc fails or takes memory promised elsewhere. It allocates nothing:
  * the page cache its kernel uses (page table, slots, counters) lives in a
- * 32 MiB static device array that every GPU loading this library holds until
- * the process exits; the store's own cache is neither read nor written. The
- * store must already be initialised (by a caller that could allocate).
+ * 32 MiB static device array, held on each GPU until the process exits; the
+ * store's own cache is neither read nor written. The store must already be
+ * initialised (by a caller that could allocate).
+ * CUDA loads the array lazily: the first call on a device makes the 32 MiB
+ * resident (and looks its address up), so make that call early, before the
+ * other allocator reserves the device, and before any stream capture; later
+ * calls leave the device's free memory unchanged.
  * Each call starts from an empty cache (it clears the page table, tags and
  * counters on its stream), so pages shared by rows of one call are fetched
- * once and nothing carries over between calls. The first call on a device
- * looks the array's address up; make it before any stream capture. All calls
- * on a device share the array: calls that overlap on the GPU race. A store
- * whose range needs more than about 4M pages of page table gets
+ * once and nothing carries over between calls. Its rows, hits and misses are
+ * added to the store's counters (gids_get_stats, gids_get_cpu_access_count).
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * A store whose range needs more than about 4M pages of page table gets
  * GIDS_E_RANGE. */
 GIDS_API int gids_read_feature_noalloc(gids_store_t *s, void *out, const int64_t *idx, int64_t n, int dim,
                                        int cache_dim, uint64_t key_off, void *stream);
@@ -213,6 +223,15 @@ GIDS_API int gids_read_feature_noalloc(gids_store_t *s, void *out, const int64_t
  * node id as a page id). row_stride_elems = 0 uses the store's row layout. */
 GIDS_API int gids_set_window_buffering(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
                               uint32_t row_stride_elems, void *stream);
+/* Takes back the marks gids_set_window_buffering made for the same rows (one
+ * pin per row and page, saturating at 0): call it for a marked minibatch that
+ * will not be gathered (an abandoned window), whose pins would otherwise keep
+ * its pages from being evicted for good. No reference counterpart: the
+ * reference never releases a window it does not gather
+ * (page_cache_backup.h:1185-1195, 1265-1272). flush_cache and the writers drop
+ * every pin of the calling rank's shard. */
+GIDS_API int gids_unset_window_buffering(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
+                                         uint32_t row_stride_elems, void *stream);
 
 /* --------------------------------------------------- constant CPU buffer --
  * cpu_backing_buffer (gids_nvme.cu:123-139): allocate a pinned, GPU-mapped
@@ -284,7 +303,8 @@ GIDS_API int gids_store_tensor(gids_store_t *s, const void *src, uint64_t num_ro
  * counterpart (the reference writes whole pages from row 0 only). */
 GIDS_API int gids_write_range(gids_store_t *s, const void *src, uint64_t nbytes, uint64_t offset_bytes);
 /* flush_cache (gids_nvme.cu:673-677): the cache holds no dirty pages here,
- * so this drops every resident page. */
+ * so this drops every resident page and every window-buffer pin (of the
+ * calling rank's shard when the cache is sharded). */
 GIDS_API int gids_flush_cache(gids_store_t *s);
 /* Host-side read of the range through the stripe map (no reference
  * counterpart; the reference's read_tensor prints elements from a GPU

@@ -51,6 +51,7 @@ def lib():
             "gids_read_feature_multi": (i32, [vp, i32, P(vp), P(vp), P(u64), i32, i32, P(u64), vp]),
             "gids_read_feature_noalloc": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
             "gids_set_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
+            "gids_unset_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_cpu_backing_buffer": (i32, [vp, u64, u64]),
             "gids_set_cpu_buffer": (i32, [vp, vp, i32]),
             "gids_set_cpu_buffer_host": (i32, [vp, vp, i64]),
@@ -76,6 +77,7 @@ def lib():
             "gids_store_ipc_handle": (i32, [vp, vp, ctypes.c_size_t]),
             "gids_store_open_peers": (i32, [vp, vp, i32]),
             "gids_store_share_shards": (i32, [P(vp), i32]),
+            "gids_store_peer_copy_gbs": (i32, [vp, i32, u64, P(ctypes.c_double)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

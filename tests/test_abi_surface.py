@@ -4,6 +4,7 @@ import ctypes
 import inspect
 import os
 import subprocess
+import sys
 
 import pytest
 
@@ -95,3 +96,16 @@ def test_gids_surface(built):
         assert hasattr(GIDS.GIDS, m), m
     params = list(inspect.signature(GIDS.GIDS_DGLDataLoader).parameters)
     assert params[:6] == ["graph", "indices", "graph_sampler", "batch_size", "dim", "GIDS"]
+
+
+def test_package_import_maps_no_library():
+    """Importing GIDS, its synthetic graphs and the bench loads none of the
+    compiled libraries (the bench's reference arm must run the reference's CPU
+    gather with nothing of this library mapped); constructing a GIDS does."""
+    code = ("import sys; sys.path[:0] = [%r, %r]; import GIDS, GIDS.synthetic, bench; "
+            "maps = open('/proc/self/maps').read(); "
+            "print('libgids_b200' in maps, 'BAM_Feature_Store' in maps)") % (
+        os.path.dirname(os.path.dirname(gids_abi.LIB_PATH)), os.path.dirname(os.path.dirname(os.path.dirname(
+            gids_abi.LIB_PATH))))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True).stdout.split()
+    assert out == ["False", "False"]

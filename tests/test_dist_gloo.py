@@ -28,7 +28,6 @@ def _worker(rank, world, port, q):
         # sharded GIDS handle exchange with a fake store
         import torch
 
-        gmod = sys.modules["GIDS.GIDS"] if "GIDS.GIDS" in sys.modules else None
         import GIDS  # noqa: F401
 
         gmod = sys.modules["GIDS.GIDS"]
@@ -56,8 +55,10 @@ def _worker(rank, world, port, q):
             def open_peers(self, handles):
                 self.calls.append(("open_peers", list(handles)))
 
-        gmod._STORE_CLASSES = {torch.float32: FakeStore}
-        gmod.BAM_Feature_Store.GIDS_Controllers = FakeCtrl
+        import types
+
+        gmod._feature_store_module = lambda: types.SimpleNamespace(BAM_Feature_Store_float=FakeStore,
+                                                                   GIDS_Controllers=FakeCtrl)
         g = gmod.GIDS(page_size=4096, cache_dim=64, num_ele=1000 * 64, shard_cache=True)
         names = [c[0] for c in g.BAM_FS.calls]
         opened = [c for c in g.BAM_FS.calls if c[0] == "open_peers"][0][1]

@@ -90,8 +90,11 @@ class FakeStore:
 
 @pytest.fixture
 def fake(monkeypatch):
-    monkeypatch.setattr(gmod, "_STORE_CLASSES", {torch.float32: FakeStore, torch.int64: FakeStore})
-    monkeypatch.setattr(gmod.BAM_Feature_Store, "GIDS_Controllers", FakeControllers)
+    import types
+
+    fake_mod = types.SimpleNamespace(BAM_Feature_Store_float=FakeStore, BAM_Feature_Store_long=FakeStore,
+                                     GIDS_Controllers=FakeControllers)
+    monkeypatch.setattr(gmod, "_feature_store_module", lambda: fake_mod)
     monkeypatch.setattr(gmod, "_current_stream_handle", lambda d: 0)
     FakeStore.table = oracle.synth_table(oracle.KIND_F32_UNIFORM, 1, 1000, 64)
 

@@ -128,3 +128,43 @@ def test_policy_arguments(table):
     assert L.gids_store_set_cache_policy(s.s, 1, 256) == gids_abi.GIDS_E_INVAL
     check(L.gids_store_set_cache_policy(s.s, 0, 2))
     s.close()
+
+
+def _mark(s, ids, times=1, unset=False):
+    L = gids_abi.lib()
+    d = torch.as_tensor(ids, dtype=torch.int64).cuda()
+    f = L.gids_unset_window_buffering if unset else L.gids_set_window_buffering
+    for _ in range(times):
+        check(f(s.s, ctypes.c_void_p(d.data_ptr()), len(ids), 0, 0, None))
+    torch.cuda.synchronize()
+
+
+def test_abandoned_window_no_longer_blocks_eviction(table):
+    # a 256-slot cache whose every line is pinned by a window that is marked
+    # but never gathered: a miss finds no victim and reads through
+    s = make(table, 1)
+    s.set_policy(False, 1)  # insert every miss (the reference's rule), second-chance clock
+    a = np.arange(0, 256)
+    _mark(s, a, times=2)  # this batch, and a later batch that will be abandoned
+    assert run(s, table, a)["miss"] == 256  # fills every slot, consumes one pin of each line
+    st = run(s, table, np.arange(1000, 1256))
+    assert (st["evictions"], st["bypass"], st["miss"]) == (0, 256, 0)
+    # the abandoned window's marks are taken back: its lines can go
+    _mark(s, a, unset=True)
+    _mark(s, a, unset=True)  # saturates at zero
+    st = run(s, table, np.arange(2000, 2256))
+    assert (st["evictions"], st["miss"], st["bypass"]) == (256, 256, 0)
+    s.close()
+
+
+def test_flush_cache_drops_window_pins(table):
+    s = make(table, 1)
+    s.set_policy(False, 1)
+    a = np.arange(0, 256)
+    _mark(s, a, times=3)
+    assert run(s, table, a)["miss"] == 256  # 2 pins left on each line
+    check(gids_abi.lib().gids_flush_cache(s.s))  # drops the lines and their pins
+    assert run(s, table, a)["miss"] == 256  # refilled; pins would now be 1 without the flush's clear
+    st = run(s, table, np.arange(2000, 2256))
+    assert (st["evictions"], st["miss"], st["bypass"]) == (256, 256, 0)
+    s.close()

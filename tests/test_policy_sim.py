@@ -1,4 +1,5 @@
-"""The page-cache policy simulator (gids-study_b200/policy_sim/cachesim.c)
+"""The page-cache policy simulator (tests/policy_sim/cachesim.c, a design-time
+tool kept with the tests)
 compiles and replays known traces to known hit ratios: a cache that holds
 every line hits on every repeat; admission makes a line's first two misses
 read through once the cache is full; a one-slot cache never hits on
@@ -10,8 +11,7 @@ import subprocess
 import numpy as np
 import pytest
 
-SIM = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "gids-study_b200", "policy_sim",
-                   "cachesim.c")
+SIM = os.path.join(os.path.dirname(os.path.abspath(__file__)), "policy_sim", "cachesim.c")
 
 
 @pytest.fixture(scope="module")

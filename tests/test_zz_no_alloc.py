@@ -105,3 +105,30 @@ def test_noalloc_rejects_a_page_table_beyond_the_scratch():
         check(L.gids_read_feature(s.s, out.data_ptr(), d.data_ptr(), 4, cdim, cdim, 0, None))  # store unaffected
     finally:
         s.close()
+
+
+def test_noalloc_leaves_free_memory_unchanged_and_counts_rows():
+    rows, cdim = 12000, 1024
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 44, rows, cdim)
+    s = Store(4, 4096, t.size, 4, num_ssd=2)
+    s.write_range(t.ctypes.data, t.nbytes, 0)
+    L = gids_abi.lib()
+    ids = np.random.default_rng(44).integers(0, rows, size=5000)
+    d = torch.as_tensor(ids, dtype=torch.int64).cuda()
+    out = torch.empty((len(ids), cdim), device="cuda")
+    try:
+        # the first call on the device loads the static array (CUDA loads it lazily)
+        check(L.gids_read_feature_noalloc(s.s, out.data_ptr(), d.data_ptr(), len(ids), cdim, cdim, 0, None))
+        torch.cuda.synchronize()
+        s.reset_stats()
+        free0 = torch.cuda.mem_get_info()[0]
+        check(L.gids_read_feature_noalloc(s.s, out.data_ptr(), d.data_ptr(), len(ids), cdim, cdim, 0, None))
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+        assert free1 == free0, f"free device memory moved by {free0 - free1} bytes"
+        assert out.cpu().numpy().tobytes() == oracle.gather(t, ids).tobytes()
+        st = s.stats()  # the call's counters are added to the store's
+        assert st["rows"] == len(ids) and st["access"] == len(ids)
+        assert st["hit"] + st["miss"] + st["bypass"] == st["access"] and st["read_io"] > 0
+    finally:
+        s.close()
