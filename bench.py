@@ -194,6 +194,30 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
+_CSC = {}
+
+
+def graph_csc(cfg, device):
+    """Explicit CSC of the config's synthetic graph on `device` (int32
+    sources), built once per process."""
+    from GIDS.synthetic import SyntheticGraph
+
+    key = (cfg["nodes"], cfg["mean_deg"], cfg["alpha"], str(device))
+    if key not in _CSC:
+        g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
+        idx_dtype = torch.int32 if cfg["nodes"] < 2**31 else torch.int64
+        _CSC[key] = g.materialize(idx_dtype)
+        del g
+    return _CSC[key]
+
+
+def use_gpu_sampler(cfg, device) -> bool:
+    """Homogeneous graphs on a GPU draw their minibatches with the CUDA
+    sampler (bit-identical to the torch sampler: tests/test_sampler_gpu.py);
+    heterographs and CPU runs use the torch sampler."""
+    return str(device) != "cpu" and not cfg["hetero"] and not cfg.get("torch_sampler")
+
+
 def batch_stream(cfg, n_batches, rank, device):
     """Input-node ids of n_batches minibatches from the seeded graph and
     sampler, produced lazily (one neighbour-sampling pass per next())."""
@@ -208,8 +232,14 @@ def batch_stream(cfg, n_batches, rank, device):
         for sd in seed_batches(h["types"][h["seed_type"]], cfg["batch"], n_batches, sampler_seed(rank), device=device):
             yield hs.sample({h["seed_type"]: sd})[0]
         return
-    g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
-    s = NeighborSampler(g, cfg["fanouts"], seed=sampler_seed(rank))
+    if use_gpu_sampler(cfg, device):
+        from GIDS.sampler import GPUNeighborSampler
+
+        indptr, indices = graph_csc(cfg, device)
+        s = GPUNeighborSampler(indptr, indices, cfg["fanouts"], seed=sampler_seed(rank), max_seeds=cfg["batch"])
+    else:
+        g = SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device)
+        s = NeighborSampler(g, cfg["fanouts"], seed=sampler_seed(rank))
     for sd in seed_batches(cfg["nodes"], cfg["batch"], n_batches, sampler_seed(rank), device=device,
                            zipf_alpha=cfg["seed_zipf"]):
         yield s.sample(sd)[0]
@@ -252,14 +282,15 @@ def time_sampler(cfg, n, rank, device, side):
 
 def make_batches(cfg, n_batches, rank, device, with_pins=False):
     """Input-node ids of n_batches minibatches from the seeded graph and
-    sampler, and (with_pins) the PageRank pin list of the constant CPU buffer."""
-    from GIDS.synthetic import SyntheticGraph, pagerank_pin_list
-
+    sampler, and (with_pins) the PageRank pin list of the constant CPU buffer
+    (the float32 GPU PageRank of the graph's CSC)."""
     t0 = time.time()
     pins = None
     if with_pins and cfg["cpu_pin_frac"] > 0 and not cfg["hetero"]:
-        pins = pagerank_pin_list(SyntheticGraph(cfg["nodes"], cfg["mean_deg"], cfg["alpha"], seed=0, device=device),
-                                 cfg["cpu_pin_frac"])
+        from GIDS.sampler import pagerank_pin_list
+
+        indptr, indices = graph_csc(cfg, device)
+        pins = pagerank_pin_list(indptr, indices, cfg["cpu_pin_frac"])
     out = list(batch_stream(cfg, n_batches, rank, device))
     if device != "cpu":
         torch.cuda.synchronize()
@@ -897,6 +928,8 @@ def main():
     ap.add_argument("--cache-warmup", type=int, default=-1,
                     help="untimed minibatches (other sampler seeds) gathered before the warm-up steps; -1: "
                          "enough for about 12 cache-sizes of line references, at most 60")
+    ap.add_argument("--torch-sampler", action="store_true",
+                    help="draw minibatches with the torch sampler instead of the CUDA sampler (same ids)")
     ap.add_argument("--policy", default="admit2", choices=sorted(POLICIES),
                     help="cache replacement: admit2 = insert on the second miss + 2-bit clock; clock = insert "
                          "every miss + second-chance clock (the reference's insertion rule)")
@@ -915,6 +948,7 @@ def main():
         cfg["phys_gb"] = args.phys_gb
     if args.cache_line >= 0:
         cfg["line"] = args.cache_line
+    cfg["torch_sampler"] = args.torch_sampler
 
     dist = Dist()
     if args.impl == "reference":

@@ -160,15 +160,22 @@ class SyntheticGraph:
         off = torch.minimum(off, (cnt - 1).clamp(min=0))
         return self._order[self._class_off[c] + off]
 
-    def materialize(self):
-        """Explicit CSC (indptr, indices) of the graph (small graphs only)."""
-        v = torch.arange(self.N, device=self.device)
-        deg = self.in_degree(v)
-        indptr = torch.zeros(self.N + 1, dtype=torch.int64, device=self.device)
-        indptr[1:] = torch.cumsum(deg, 0)
-        rows = torch.repeat_interleave(v, deg)
-        j = torch.arange(int(indptr[-1]), device=self.device) - indptr[:-1].repeat_interleave(deg)
-        return indptr, self.in_neighbor(rows, j)
+    def materialize(self, index_dtype=torch.int64, chunk_rows: int = 1 << 22):
+        """Explicit CSC (indptr int64 [N+1], indices [E] of index_dtype) of the
+        graph: indices[indptr[v] + j] = in_neighbor(v, j), built chunk by
+        chunk of destination rows."""
+        dev = self.device
+        deg = self.in_degree(torch.arange(self.N, device=dev))
+        indptr = torch.zeros(self.N + 1, dtype=torch.int64, device=dev)
+        torch.cumsum(deg, 0, out=indptr[1:])
+        indices = torch.empty(int(indptr[-1]), dtype=index_dtype, device=dev)
+        for lo in range(0, self.N, chunk_rows):
+            hi = min(self.N, lo + chunk_rows)
+            d = deg[lo:hi]
+            rows = torch.repeat_interleave(torch.arange(lo, hi, device=dev), d)
+            j = torch.arange(rows.numel(), device=dev) - torch.repeat_interleave(indptr[lo:hi] - indptr[lo], d)
+            indices[int(indptr[lo]):int(indptr[hi])] = self.in_neighbor(rows, j).to(index_dtype)
+        return indptr, indices
 
 
 def unique_first(x: torch.Tensor) -> torch.Tensor:
@@ -265,46 +272,6 @@ def seed_batches(num_nodes: int, batch_size: int, n_batches: int, seed: int, dev
             s = unique_first(torch.cat([s, more]))
         out.append(s[:batch_size].to(device))
     return out
-
-
-def pagerank_pin_list(graph: SyntheticGraph, fraction: float = 0.01, damping: float = 0.85, iters: int = 20,
-                      chunk_rows: int = 1 << 22):
-    """pin_file for the constant CPU buffer: the top ``fraction`` of nodes by
-    the reference's in-degree-normalised ("reverse") PageRank.
-
-    Restates compute_pagerank (evaluation/page_rank_node_list_gen.py:126-134)
-    and the top-k of :282-285: pv = 1/N; K times: pv = pv / in_degree;
-    pv[v] = sum of pv[u] over the in-edges u -> v (copy_u + sum);
-    pv = (1 - d)/N + d * pv. The reference divides by a zero in-degree and
-    propagates inf/NaN from such nodes; here their share is 0 (guard).
-    Edges are generated and summed in chunks of ``chunk_rows`` destination
-    rows; returns the node ids, highest rank first (int64)."""
-    g = graph
-    dev = g.device
-    N = g.N
-    deg = g.in_degree(torch.arange(N, device=dev))
-    inv = torch.where(deg > 0, 1.0 / deg.clamp(min=1).to(torch.float64), torch.zeros((), dtype=torch.float64,
-                                                                                     device=dev))
-    # explicit CSC, built once per chunk of destination rows, kept as int32 sources
-    chunks = []
-    for lo in range(0, N, chunk_rows):
-        hi = min(N, lo + chunk_rows)
-        v = torch.arange(lo, hi, device=dev)
-        d = deg[lo:hi]
-        rows = torch.repeat_interleave(v, d)
-        start = torch.cumsum(d, 0) - d
-        j = torch.arange(rows.numel(), device=dev) - torch.repeat_interleave(start, d)
-        src = g.in_neighbor(rows, j)
-        chunks.append((lo, hi, (rows - lo).to(torch.int32), src.to(torch.int64 if N >= (1 << 31) else torch.int32)))
-    pv = torch.full((N,), 1.0 / N, dtype=torch.float64, device=dev)
-    for _ in range(iters):
-        norm = pv * inv
-        new = torch.zeros_like(pv)
-        for lo, hi, rows, src in chunks:
-            new[lo:hi].index_add_(0, rows.to(torch.int64), norm[src.to(torch.int64)])
-        pv = (1.0 - damping) / N + damping * new
-    k = max(1, int(N * fraction))
-    return torch.topk(pv, k, largest=True).indices
 
 
 class HeteroSyntheticGraph:

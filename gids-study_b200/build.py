@@ -26,7 +26,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["gather.cu", "store.cu", "noalloc.cu"]
+CU_SOURCES = ["gather.cu", "store.cu", "noalloc.cu", "sampler.cu"]
 CPP_SOURCES = ["backing.cpp", "abi.cpp"]
 HEADERS = [os.path.join(CSRC, "gids_internal.hpp"), os.path.join(INCLUDE, "gids_b200.h")]
 

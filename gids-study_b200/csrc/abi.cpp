@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <memory>
 #include <new>
 #include <string>
 
@@ -15,6 +16,10 @@ struct gids_ctrls {
 struct gids_store {
   explicit gids_store(uint32_t eb, int dev) : s(eb, dev) {}
   gids::Store s;
+};
+struct gids_sampler {
+  gids::Sampler* p = nullptr;
+  ~gids_sampler() { gids::sampler_destroy(p); }
 };
 
 gids::Store* gids_store_of(gids_store_t* s) { return &s->s; }
@@ -457,6 +462,46 @@ int gids_store_geometry(gids_store_t* s, uint64_t* out, int count) {
                            s->s.n_slots, s->s.page_size,         s->s.ctrls->n_bound,
                            s->s.line_size};
     for (int i = 0; i < count && i < 7; i++) out[i] = g[i];
+  });
+}
+
+
+int gids_sampler_create(gids_sampler_t** out, int device, const int64_t* indptr, const void* indices, int index_bytes,
+                        uint64_t num_nodes, const int* fanouts, int n_layers, uint64_t max_seeds, uint64_t seed) {
+  return guarded([&] {
+    NEED(out);
+    *out = nullptr;
+    std::unique_ptr<gids_sampler> h(new gids_sampler());
+    h->p = gids::sampler_create(device, indptr, indices, index_bytes, num_nodes, fanouts, n_layers, max_seeds, seed);
+    *out = h.release();
+  });
+}
+
+int gids_sampler_capacity(gids_sampler_t* s, uint64_t* out) {
+  return guarded([&] {
+    NEED(s);
+    NEED(out);
+    *out = gids::sampler_capacity(s->p);
+  });
+}
+
+int gids_sampler_sample(gids_sampler_t* s, const int64_t* seeds, uint64_t n_seeds, int64_t* out_nodes,
+                        uint64_t out_cap, uint64_t* count_dev, uint64_t* count_host, int64_t call, void* stream) {
+  return guarded([&] {
+    NEED(s);
+    gids::sampler_sample(s->p, seeds, n_seeds, out_nodes, out_cap, count_dev, count_host, call, (cudaStream_t)stream);
+  });
+}
+
+int gids_sampler_destroy(gids_sampler_t* s) {
+  return guarded([&] { delete s; });
+}
+
+int gids_pagerank(int device, const int64_t* indptr, const void* indices, int index_bytes, uint64_t num_nodes,
+                  int iters, double damping, float* pv, uint64_t* order_keys, void* stream) {
+  return guarded([&] {
+    gids::pagerank(device, indptr, indices, index_bytes, num_nodes, iters, damping, pv, order_keys,
+                   (cudaStream_t)stream);
   });
 }
 

@@ -344,6 +344,35 @@ void bind_store(py::module_& m, const char* name) {
 
 }  // namespace
 
+// extension: the GPU neighbour sampler over a CSC graph (gids_sampler_*)
+class Sampler {
+ public:
+  Sampler(int device, uint64_t indptr, uint64_t indices, int index_bytes, uint64_t num_nodes,
+          const std::vector<int>& fanouts, uint64_t max_seeds, uint64_t seed) {
+    check(gids_sampler_create(&s_, device, (const int64_t*)indptr, (const void*)indices, index_bytes, num_nodes,
+                              fanouts.data(), (int)fanouts.size(), max_seeds, seed));
+  }
+  ~Sampler() {
+    if (s_) gids_sampler_destroy(s_);
+  }
+  uint64_t capacity() {
+    uint64_t v = 0;
+    check(gids_sampler_capacity(s_, &v));
+    return v;
+  }
+  // returns the node count (waits for the stream) unless count_dev is given
+  uint64_t sample(uint64_t seeds, uint64_t n_seeds, uint64_t out, uint64_t out_cap, uint64_t count_dev, int64_t call,
+                  uint64_t stream) {
+    uint64_t host = 0;
+    check(gids_sampler_sample(s_, (const int64_t*)seeds, n_seeds, (int64_t*)out, out_cap, (uint64_t*)count_dev,
+                              count_dev ? nullptr : &host, call, (void*)stream));
+    return host;
+  }
+
+ private:
+  gids_sampler_t* s_ = nullptr;
+};
+
 PYBIND11_MODULE(BAM_Feature_Store, m) {
   m.doc() = "B200 GIDS feature store (drop-in for the reference's BAM_Feature_Store pybind module)";
   py::class_<Controllers>(m, "GIDS_Controllers")
@@ -365,6 +394,25 @@ PYBIND11_MODULE(BAM_Feature_Store, m) {
   bind_store<2, 0>(m, "BAM_Feature_Store_half");
   bind_store<2, 1>(m, "BAM_Feature_Store_bfloat16");
   m.def("version", []() { return std::string(gids_version()); });
+  py::class_<Sampler>(m, "GIDS_Sampler")
+      .def(py::init<int, uint64_t, uint64_t, int, uint64_t, const std::vector<int>&, uint64_t, uint64_t>(),
+           py::arg("device"), py::arg("indptr"), py::arg("indices"), py::arg("index_bytes"), py::arg("num_nodes"),
+           py::arg("fanouts"), py::arg("max_seeds"), py::arg("seed"))
+      .def("capacity", &Sampler::capacity)
+      .def("sample", &Sampler::sample, py::arg("seeds"), py::arg("n_seeds"), py::arg("out"), py::arg("out_cap"),
+           py::arg("count_dev") = 0, py::arg("call") = -1, py::arg("stream") = 0,
+           py::call_guard<py::gil_scoped_release>());
+  // extension: compute_pagerank of the pin-list generator in float32 (gids_pagerank)
+  m.def(
+      "pagerank",
+      [](int device, uint64_t indptr, uint64_t indices, int index_bytes, uint64_t n, int iters, double damping,
+         uint64_t pv, uint64_t keys, uint64_t stream) {
+        check(gids_pagerank(device, (const int64_t*)indptr, (const void*)indices, index_bytes, n, iters, damping,
+                            (float*)pv, (uint64_t*)keys, (void*)stream));
+      },
+      py::arg("device"), py::arg("indptr"), py::arg("indices"), py::arg("index_bytes"), py::arg("num_nodes"),
+      py::arg("iters"), py::arg("damping"), py::arg("pv"), py::arg("keys") = 0, py::arg("stream") = 0,
+      py::call_guard<py::gil_scoped_release>());
   // extension: one process driving every GPU of a sharded cache
   m.def("share_shards", [](py::list stores) {
     std::vector<gids_store_t*> v;

@@ -163,6 +163,17 @@ void launch_wb_mark(const WbArgs& a, cudaStream_t st);
 int gather_blocks_per_sm(int vec, bool sys);
 constexpr int GATHER_THREADS = 256;
 
+// Neighbour sampler and pin-list PageRank (sampler.cu).
+struct Sampler;
+Sampler* sampler_create(int device, const int64_t* indptr, const void* indices, int index_bytes, uint64_t n_nodes,
+                        const int* fanouts, int n_layers, uint64_t max_seeds, uint64_t seed);
+void sampler_destroy(Sampler* s);
+uint64_t sampler_capacity(const Sampler* s);
+void sampler_sample(Sampler* s, const int64_t* seeds, uint64_t n_seeds, int64_t* out_nodes, uint64_t out_cap,
+                    uint64_t* count_dev, uint64_t* host_count, int64_t call, cudaStream_t st);
+void pagerank(int device, const int64_t* indptr, const void* indices, int index_bytes, uint64_t n, int iters,
+              double damping, float* pv, uint64_t* keys, cudaStream_t st);
+
 // ------------------------------------------------------- emulated SSDs
 struct SsdRegion {
   char* host = nullptr;

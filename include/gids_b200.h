@@ -322,6 +322,50 @@ GIDS_API int gids_fill_synthetic(gids_store_t *s, int kind, uint64_t seed, int t
  * [4]=page size, [5]=number of SSDs, [6]=cache line size. */
 GIDS_API int gids_store_geometry(gids_store_t *s, uint64_t *out, int count);
 
+/* ------------------------------------------------------------- sampler --
+ * The minibatches fed to fetch_feature: replaces the DGL
+ * MultiLayerNeighborSampler that feeds the reference's loader
+ * (GIDS_Setup/GIDS/GIDS.py:178-201, evaluation/homogenous_train.py:201-203)
+ * with a GPU sampler over a CSC graph held on the sampler's GPU: indptr is
+ * int64 [num_nodes + 1], indices int32 or int64 (index_bytes 4 or 8) [edges];
+ * in-edges of v are indices[indptr[v] .. indptr[v+1]). Both arrays must
+ * outlive the sampler. fanouts[0..n_layers) as in DGL (fanouts[0] is the
+ * layer nearest the input; hops run from the last fanout to the first), each
+ * in [1, 32]. Each hop keeps, for every node of the current set, the
+ * min(fanout, in-degree) in-edges of smallest counter-hashed key (a function
+ * of seed, call index, hop, node and edge index), and appends the new sources
+ * in order of first appearance; the result (seeds first, duplicates removed)
+ * is the minibatch's input_nodes, bit-identical to the torch restatement in
+ * GIDS/synthetic.py on any device. max_seeds bounds the seeds of one call.
+ * gids_sampler_capacity: the output capacity a call needs (nodes).
+ * gids_sampler_sample: runs on `stream` without a host synchronisation;
+ * count_dev (device uint64, may be NULL) receives the node count; count_host
+ * (may be NULL) makes the call wait and return it there. call < 0 uses the
+ * sampler's own call counter (0, 1, 2, ...); a seed outside the graph gives
+ * GIDS_E_RANGE (with count_host). */
+typedef struct gids_sampler gids_sampler_t;
+GIDS_API int gids_sampler_create(gids_sampler_t **out, int device, const int64_t *indptr, const void *indices,
+                                 int index_bytes, uint64_t num_nodes, const int *fanouts, int n_layers,
+                                 uint64_t max_seeds, uint64_t seed);
+GIDS_API int gids_sampler_capacity(gids_sampler_t *s, uint64_t *out);
+GIDS_API int gids_sampler_sample(gids_sampler_t *s, const int64_t *seeds, uint64_t n_seeds, int64_t *out_nodes,
+                                 uint64_t out_cap, uint64_t *count_dev, uint64_t *count_host, int64_t call,
+                                 void *stream);
+GIDS_API int gids_sampler_destroy(gids_sampler_t *s);
+
+/* The pin list of the constant CPU buffer: compute_pagerank of
+ * evaluation/page_rank_node_list_gen.py:126-134 on the GPU, in float32 --
+ * pv = 1/N; `iters` times: pv = pv / in_degree; pv[v] = sum of pv[u] over the
+ * in-edges u -> v (in CSC order, one float32 add at a time); pv = (1-d)/N +
+ * d * pv -- into pv[num_nodes] (device). Nodes without in-edges contribute 0
+ * (the reference divides by zero there). With order_keys (device uint64
+ * [num_nodes], may be NULL), also writes one key per node whose ascending
+ * order is pv descending, node id ascending: the pin_file is the node ids
+ * (key & 0xffffffff) of the k smallest keys (page_rank_node_list_gen.py:282-285
+ * takes torch.topk of pv). */
+GIDS_API int gids_pagerank(int device, const int64_t *indptr, const void *indices, int index_bytes, uint64_t num_nodes,
+                           int iters, double damping, float *pv, uint64_t *order_keys, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

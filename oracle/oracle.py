@@ -1,4 +1,4 @@
-"""CPU oracle for the GIDS feature gather (test infrastructure only).
+"""CPU oracle for the GIDS feature gather and its inputs (test infrastructure only).
 
 Only tests/, the smoke entry point and the bench's CPU-baseline leg import this
 module; the product never does. It wraps the plain-C restatement in
@@ -57,6 +57,16 @@ def lib():
         L.go_stripe_locate.argtypes = [u64, u64, u64, u64, ctypes.POINTER(u64), ctypes.POINTER(u64)]
         L.go_stripe_image.restype = i32
         L.go_stripe_image.argtypes = [vp, u64, u32, u64, u64, ctypes.POINTER(vp), u64]
+        L.go_hop_seed.restype = u64
+        L.go_hop_seed.argtypes = [u64, u64, u64]
+        L.go_edge_key.restype = u64
+        L.go_edge_key.argtypes = [u64, u64, u64]
+        L.go_sample.restype = i64
+        L.go_sample.argtypes = [vp, vp, i32, u64, vp, i32, vp, u64, u64, u64, vp, u64]
+        L.go_pagerank_f32.restype = i32
+        L.go_pagerank_f32.argtypes = [vp, vp, i32, u64, i32, ctypes.c_double, vp]
+        L.go_topk_desc.restype = i32
+        L.go_topk_desc.argtypes = [vp, u64, u64, vp]
         _lib = L
     return _lib
 
@@ -127,6 +137,57 @@ def stripe_image(logical: np.ndarray, page_size: int, n_ctrls: int, page_start: 
     rc = lib().go_stripe_image(logical.ctypes.data, logical.size, page_size, n_ctrls, page_start, ptrs, dev_bytes)
     assert rc == 0, rc
     return devs
+
+
+# ------------------------------------------------------------------ sampler and pin list
+def hop_seed(seed: int, call: int, hop: int) -> int:
+    return lib().go_hop_seed(seed & (2**64 - 1), call, hop)
+
+
+def edge_key(seed_h: int, v: int, j: int) -> int:
+    return lib().go_edge_key(seed_h & (2**64 - 1), v, j)
+
+
+def _csc(indptr, indices):
+    indptr = np.ascontiguousarray(indptr, dtype=np.int64)
+    indices = np.ascontiguousarray(indices)
+    assert indices.dtype in (np.int32, np.int64)
+    return indptr, indices, indices.dtype.itemsize
+
+
+def sample(indptr, indices, fanouts, seeds, seed: int, call: int = 0) -> np.ndarray:
+    """Restated MultiLayerNeighborSampler with counter-hashed edge choice
+    (sampler_oracle.c): the input nodes of one minibatch, seeds first."""
+    indptr, indices, ib = _csc(indptr, indices)
+    n = indptr.shape[0] - 1
+    f = np.ascontiguousarray(fanouts, dtype=np.int32)
+    seeds = np.ascontiguousarray(seeds, dtype=np.int64)
+    cap = max(1, n)
+    out = np.empty(cap, dtype=np.int64)
+    rc = lib().go_sample(indptr.ctypes.data, indices.ctypes.data, ib, n, f.ctypes.data, len(f), seeds.ctypes.data,
+                         len(seeds), seed & (2**64 - 1), call, out.ctypes.data, cap)
+    if rc == -2:
+        raise IndexError("seed outside the graph")
+    assert rc >= 0, rc
+    return out[:rc].copy()
+
+
+def pagerank_f32(indptr, indices, iters: int = 20, damping: float = 0.85) -> np.ndarray:
+    """compute_pagerank (page_rank_node_list_gen.py:126-134) restated in float32 (sampler_oracle.c)."""
+    indptr, indices, ib = _csc(indptr, indices)
+    n = indptr.shape[0] - 1
+    pv = np.empty(n, dtype=np.float32)
+    rc = lib().go_pagerank_f32(indptr.ctypes.data, indices.ctypes.data, ib, n, iters, damping, pv.ctypes.data)
+    assert rc == 0, rc
+    return pv
+
+
+def topk_desc(pv: np.ndarray, k: int) -> np.ndarray:
+    """Node ids of the k largest values, value descending then id ascending."""
+    pv = np.ascontiguousarray(pv, dtype=np.float32)
+    out = np.empty(k, dtype=np.int64)
+    assert lib().go_topk_desc(pv.ctypes.data, pv.shape[0], k, out.ctypes.data) == 0
+    return out
 
 
 # ------------------------------------------------------------------ mmap baseline

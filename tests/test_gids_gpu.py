@@ -72,8 +72,8 @@ def test_window_buffering_fetch(table):
     # abandon the window (its marks are taken back) and start a fresh iterator
     g.drop_window_buffer()
     assert g.window_buffer == [] and not g.wb_init
-    fresh = homo_batches(4, 2500, 3)
-    check_homo(table, run(g, fresh, 4, CDIM), fresh, CDIM)
+    fresh = homo_batches(7, 2500, 3)  # the refilled window reads 3 batches ahead
+    check_homo(table, run(g, fresh, 4, CDIM), fresh[:4], CDIM)
     g.close()
 
 

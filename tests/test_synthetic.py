@@ -1,10 +1,10 @@
-"""Synthetic graph, neighbour sampler and PageRank pin list (the inputs of the
-benchmarks), checked on CPU against an explicit CSC of the same graph."""
+"""Synthetic graph and neighbour sampler (the inputs of the benchmarks),
+checked on CPU against an explicit CSC of the same graph."""
 import numpy as np
 import torch
 
-from GIDS.synthetic import (NeighborSampler, SyntheticGraph, edge_key, hop_seed, pagerank_pin_list, seed_batches,
-                            unique_first, zipf_truncation)
+from GIDS.synthetic import (NeighborSampler, SyntheticGraph, edge_key, hop_seed, seed_batches, unique_first,
+                            zipf_truncation)
 
 
 def test_zipf_truncation_reaches_mean():
@@ -70,25 +70,6 @@ def test_zipf_seeds_are_skewed():
     assert s.numel() == 4000 and torch.unique(s).numel() == 4000
 
 
-def test_pagerank_pin_list_matches_dense_restatement():
-    g = SyntheticGraph(15000, 15, 1.2, seed=1)
-    pins = pagerank_pin_list(g, 0.02, chunk_rows=4000)
-    ip, ind = g.materialize()
-    N = g.N
-    deg = (ip[1:] - ip[:-1]).numpy().astype(np.float64)
-    rows = np.repeat(np.arange(N), (ip[1:] - ip[:-1]).numpy())
-    src = ind.numpy()
-    pv = np.full(N, 1.0 / N)
-    for _ in range(20):  # page_rank_node_list_gen.py:126-134, zero in-degree guarded
-        norm = np.where(deg > 0, pv / np.maximum(deg, 1), 0.0)
-        new = np.zeros(N)
-        np.add.at(new, rows, norm[src])
-        pv = 0.15 / N + 0.85 * new
-    top = np.argsort(-pv, kind="stable")[: int(N * 0.02)]
-    assert set(top.tolist()) == set(pins.tolist())
-    assert pv[pins[0].item()] == pv.max()
-
-
 def test_bench_batch_stream_is_the_batch_list():
     """bench.py's lazy sampler stream yields the same minibatches as its list
     form (the timed steps and the loader measurement draw from the same law)."""
@@ -125,3 +106,10 @@ def test_sampler_calls_draw_fresh_minibatches():
     a = s.sample(sd)[0]
     b = s.sample(sd)[0]  # same seeds, next call: other edges
     assert not torch.equal(a, b) and torch.equal(a[:64], b[:64])
+
+
+def test_chunked_csc_equals_one_chunk():
+    g = SyntheticGraph(30000, 15, 1.1, seed=2)
+    ip, ind = g.materialize()
+    ip2, ind2 = g.materialize(torch.int32, chunk_rows=7000)
+    assert torch.equal(ip, ip2) and ind2.dtype == torch.int32 and torch.equal(ind, ind2.long())
