@@ -13,12 +13,13 @@
  *                  ("warp32", the first kernel) or m = lines still to place,
  *                  doubling per round ("warpN", the current kernel).
  * Admission (window W, in multiples of the total slots; 0 = off): once a
- * shard's hand has gone round, a line's first miss since the last clear of
- * the admission bits does not insert it. ref_max: clock chances added per hit.
+ * shard's hand has gone round, a line is inserted only on its A-th miss since
+ * the last clear of the admission counts (A = 2 by default: the first miss
+ * reads through). ref_max: clock chances added per hit.
  *
  * Build: gcc -O2 -o cachesim cachesim.c
  * Run:   cachesim trace.npy trace_len.npy n_lines slots_per_shard \
- *                 policy,shards,ref_max,window ...
+ *                 policy,shards,ref_max,window[,admit] ...
  *        e.g. cachesim t.npy t_len.npy 100000000 10485760 warpN,1,3,2 seq,1,1,0
  */
 #include <stdint.h>
@@ -46,22 +47,22 @@ static void* load_npy(const char* path, long* n) {
   return b + o;
 }
 
-static void run(const char* policy, int S, int K, double W) {
+static void run(const char* policy, int S, int K, double W, int A) {
   const int warp = strncmp(policy, "warp", 4) == 0;
   const int m32 = strcmp(policy, "warp32") == 0;
   int32_t* state = malloc(nlines * 4);  /* slot within the owner's shard, or -1 */
   int32_t* tag = malloc(S * nslots * 4);
   uint8_t* ref = calloc(S * nslots, 1);
-  uint64_t* seen = calloc(nlines / 64 + 1, 8);
+  uint8_t* seen = calloc(nlines + 1, 1);  /* misses of each line in the window */
   memset(state, 0xff, nlines * 4);
   memset(tag, 0xff, S * nslots * 4);
   int64_t hand[64] = {0}, since = 0, pos = 0;
-  printf("%s shards=%d ref_max=%d window=%.1f:", policy, S, K, W);
+  printf("%s shards=%d ref_max=%d window=%.1f admit=%d:", policy, S, K, W, A);
   for (int b = 0; b < nb; b++) {
     const int64_t n = lens[b];
     int64_t hits = 0;
     since += n;
-    if (W > 0 && since > W * nslots * S) { memset(seen, 0, (nlines / 64 + 1) * 8); since = n; }
+    if (W > 0 && since > W * nslots * S) { memset(seen, 0, nlines + 1); since = n; }
     int gate[64];
     for (int r = 0; r < S; r++) gate[r] = W > 0 && hand[r] >= nslots;  /* read once per launch */
     const int64_t chunk = warp ? 32 : 1;
@@ -79,9 +80,8 @@ static void run(const char* policy, int S, int K, double W) {
           continue;
         }
         if (gate[r]) {
-          const uint64_t bit = 1ull << (l & 63), old = seen[l >> 6];
-          seen[l >> 6] |= bit;
-          if (!(old & bit)) continue;  /* first miss: read through, not inserted */
+          if (seen[l] < 255) seen[l]++;
+          if (seen[l] < A) continue;  /* an early miss: read through, not inserted */
         }
         own[no++] = l;
       }
@@ -132,10 +132,11 @@ int main(int argc, char** argv) {
   nslots = atol(argv[4]);
   for (int a = 5; a < argc; a++) {
     char pol[16];
-    int S, K;
+    int S, K, A = 2;
     double W;
-    if (sscanf(argv[a], "%15[^,],%d,%d,%lf", pol, &S, &K, &W) != 4 || S < 1 || S > 64) { fprintf(stderr, "bad spec %s\n", argv[a]); return 2; }
-    run(pol, S, K, W);
+    const int got = sscanf(argv[a], "%15[^,],%d,%d,%lf,%d", pol, &S, &K, &W, &A);
+    if (got < 4 || S < 1 || S > 64 || A < 1) { fprintf(stderr, "bad spec %s\n", argv[a]); return 2; }
+    run(pol, S, K, W, A);
   }
   return 0;
 }
