@@ -633,6 +633,9 @@ def run_ours(args, cfg, dist: Dist):
 
     hbm_peak, hbm_src = measured_hbm_peak()
     host_peak = host_link_peak_gbs(device, dist)
+    # the link at the cache's own access size: random line reads from the emulated SSDs
+    line_b = int(geo.get("cache_line", page))
+    host_rand = bam.host_read_gbs(min(line_b, 4096), 4 << 30)
     nvlink_peak = None
     if g.world > 1:
         # every rank copies 1 GiB from the next rank's shard at the same time
@@ -775,7 +778,11 @@ def run_ours(args, cfg, dist: Dist):
         "hbm": {"alg_bytes_per_launch": int(alg_hbm), "achieved_gbs": round(alg_hbm / t_launch / 1e9, 1),
                 "peak_gbs": hbm_peak},
         "host_link": {"alg_bytes_per_launch": int(r_host), "achieved_gbs": round(r_host / t_launch / 1e9, 2),
-                      "peak_gbs": round(host_peak, 2)},
+                      "peak_gbs": round(host_peak, 2),
+                      "random_read_gbs": round(host_rand, 2),
+                      "random_read_method": f"random {min(line_b, 4096)}-byte reads from the start of cache lines of "
+                                            "the emulated SSDs, 4 GiB, best of 3 (gids_store_host_read_gbs)",
+                      "frac_of_random_read": round(r_host / t_launch / 1e9 / host_rand, 4) if host_rand else None},
         "mix": {"hit": round(st["hit"] / acc, 4), "miss": round(st["miss"] / acc, 4),
                 "bypass": round(st["bypass"] / acc, 4), "cpu_rows": st["cpu_rows"],
                 "peer_bytes_frac": round(st.get("bytes_peer", 0) / max(1, st["rows"] * row_bytes), 4)},

@@ -285,6 +285,14 @@ int gids_store_peer_copy_gbs(gids_store_t* s, int peer, uint64_t bytes, double* 
   });
 }
 
+int gids_store_host_read_gbs(gids_store_t* s, uint32_t read_bytes, uint64_t total_bytes, double* out) {
+  return guarded([&] {
+    NEED(s);
+    NEED(out);
+    *out = s->s.host_read_gbs(read_bytes, total_bytes);
+  });
+}
+
 int gids_read_feature(gids_store_t* s, void* out, const int64_t* idx, int64_t n, int dim, int cache_dim,
                       uint64_t key_off, void* stream) {
   return guarded([&] {

@@ -200,6 +200,12 @@ class FeatureStore {
     check(gids_store_peer_copy_gbs(s(), peer, bytes, &v));
     return v;
   }
+  // host-link bandwidth of random reads at the gather's access size (GB/s)
+  double host_read_gbs(uint32_t read_bytes, uint64_t total_bytes) {
+    double v = 0.0;
+    check(gids_store_host_read_gbs(s(), read_bytes, total_bytes, &v));
+    return v;
+  }
   py::bytes ipc_handle() {
     char h[64];
     check(gids_store_ipc_handle(s(), h, sizeof(h)));
@@ -327,6 +333,7 @@ void bind_store(py::module_& m, const char* name) {
       .def("set_gather_blocks", &S::set_gather_blocks, py::arg("max_blocks"))
       .def("ipc_handle", &S::ipc_handle)
       .def("peer_copy_gbs", &S::peer_copy_gbs, py::arg("peer"), py::arg("bytes"), R())
+      .def("host_read_gbs", &S::host_read_gbs, py::arg("read_bytes"), py::arg("total_bytes"), R())
       .def("open_peers", &S::open_peers)
       .def("set_synchronous", &S::set_synchronous, R())
       .def("set_row_layout", &S::set_row_layout, R())

@@ -973,7 +973,48 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   }
 }
 
+// Host-link probe: every warp reads `read_bytes` (512, 1024, 2048 or 4096)
+// from the start of pseudo-random lines of the backing store, eight 16-byte
+// vectors in flight per lane as in the gather's host copies, and stores them
+// to a device buffer. Measures what the link delivers for the gather's own
+// access size and footprint.
+__global__ void __launch_bounds__(GATHER_THREADS, 2)
+    host_probe_kernel(const DevBacking b, uint64_t n_lines, uint32_t line_shift, uint32_t read_bytes,
+                      uint64_t reads, int4* __restrict__ dst, uint64_t dst_vecs, uint64_t seed) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t per_round = 32u * 16u * INFLIGHT / read_bytes;  // reads per 4 KB round of a warp (>= 1)
+  const uint32_t vecs = read_bytes / 16u;
+  const uint64_t w = (uint64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
+  const uint64_t nw = (uint64_t)gridDim.x * WARPS;
+  for (uint64_t r = w; r * per_round < reads; r += nw) {
+    int4 v[INFLIGHT];
+#pragma unroll
+    for (int q = 0; q < INFLIGHT; q++) {
+      const uint32_t e = (uint32_t)q * 32u + (uint32_t)lane;  // vector index within the round
+      const uint64_t k = r * per_round + e / vecs;             // read index
+      unsigned long long z = seed + k * 0x9E3779B97F4A7C15ull;
+      z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+      z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+      z ^= z >> 31;
+      v[q] = __ldcg(reinterpret_cast<const int4*>(backing_addr(b, z % n_lines, line_shift)) + (e % vecs));
+    }
+#pragma unroll
+    for (int q = 0; q < INFLIGHT; q++)
+      __stcs(dst + ((r * (32u * INFLIGHT) + (uint64_t)q * 32u + (uint64_t)lane) % dst_vecs), v[q]);
+  }
+}
+
 }  // namespace
+
+void launch_host_probe(const DevBacking& b, uint64_t n_lines, uint32_t line_shift, uint32_t read_bytes,
+                       uint64_t reads, void* dst, uint64_t dst_bytes, uint64_t seed, cudaStream_t st) {
+  int sms = 0, dev = 0;
+  GIDS_CUDA(cudaGetDevice(&dev));
+  GIDS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  host_probe_kernel<<<2 * sms, GATHER_THREADS, 0, st>>>(b, n_lines, line_shift, read_bytes, reads,
+                                                        reinterpret_cast<int4*>(dst), dst_bytes / 16, seed);
+  GIDS_CUDA(cudaGetLastError());
+}
 
 constexpr size_t kTmaRingBytes = (size_t)WARPS * TMA_STAGES * TMA_STAGE_BYTES;
 

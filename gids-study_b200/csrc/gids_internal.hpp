@@ -160,6 +160,8 @@ struct WbArgs {
 // state-word atomics and fences use system scope.
 void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st);
 void launch_wb_mark(const WbArgs& a, cudaStream_t st);
+void launch_host_probe(const DevBacking& b, uint64_t n_lines, uint32_t line_shift, uint32_t read_bytes,
+                       uint64_t reads, void* dst, uint64_t dst_bytes, uint64_t seed, cudaStream_t st);
 int gather_blocks_per_sm(int vec, bool sys);
 constexpr int GATHER_THREADS = 256;
 
@@ -292,6 +294,9 @@ class Store {
   // bandwidth of a device-to-device copy of `bytes` from rank `peer`'s shard
   // into this GPU (GB/s, best of three): the link term of the roofline
   double peer_copy_gbs(uint32_t peer, uint64_t bytes);
+  // host-link bandwidth of random reads of `read_bytes` from the start of
+  // cache lines of the backing store (GB/s, best of three launches)
+  double host_read_gbs(uint32_t read_bytes, uint64_t total_bytes);
 
   // device allocations (this rank's shard lives in one allocation, d_shard)
   char* d_shard = nullptr;

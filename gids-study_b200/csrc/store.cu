@@ -704,6 +704,45 @@ double Store::peer_copy_gbs(uint32_t peer, uint64_t bytes) {
   return best;
 }
 
+double Store::host_read_gbs(uint32_t read_bytes, uint64_t total_bytes) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(initialized, GIDS_E_STATE, "host_read_gbs before init_controllers");
+  GIDS_CHECK(read_bytes >= 512 && read_bytes <= 4096 && 4096 % read_bytes == 0 && read_bytes <= line_size,
+             GIDS_E_INVAL, "read size must be 512, 1024, 2048 or 4096 bytes and at most one cache line");
+  DeviceGuard g(device);
+  const uint64_t dst_bytes = 256ull << 20;
+  const uint64_t reads = std::max<uint64_t>(1, total_bytes / read_bytes);
+  // lines that lie in the physically held pages
+  const uint64_t lines = std::min<uint64_t>(n_lines, ctrls->wrap_pages << (page_shift - line_shift));
+  char* dst = nullptr;
+  cudaEvent_t a = nullptr, b = nullptr;
+  double best = 0.0;
+  GIDS_CUDA(cudaMalloc(&dst, dst_bytes));
+  try {
+    GIDS_CUDA(cudaEventCreate(&a));
+    GIDS_CUDA(cudaEventCreate(&b));
+    for (int rep = 0; rep < 4; rep++) {  // the first is a warm-up
+      GIDS_CUDA(cudaEventRecord(a, 0));
+      launch_host_probe(dev_backing(), lines, line_shift, read_bytes, reads, dst, dst_bytes, 1234567ull * (rep + 1),
+                        0);
+      GIDS_CUDA(cudaEventRecord(b, 0));
+      GIDS_CUDA(cudaEventSynchronize(b));
+      float ms = 0.f;
+      GIDS_CUDA(cudaEventElapsedTime(&ms, a, b));
+      if (rep && ms > 0.f) best = std::max(best, (double)(reads * read_bytes) / 1e9 / (ms / 1e3));
+    }
+  } catch (...) {
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+    cudaFree(dst);
+    throw;
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  cudaFree(dst);
+  return best;
+}
+
 void Store::synchronize() {
   std::lock_guard<std::mutex> lk(mu);
   DeviceGuard g(device);

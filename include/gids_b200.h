@@ -172,6 +172,13 @@ GIDS_API int gids_store_share_shards(gids_store_t *const *stores, int n);
  * best of three timed copies in GB/s. Run it on every rank at once for the
  * bandwidth a rank gets while the others also use their links. */
 GIDS_API int gids_store_peer_copy_gbs(gids_store_t *s, int peer, uint64_t bytes, double *out);
+/* Host-link bandwidth at the gather's own access size (no reference
+ * counterpart; a measurement aid): total_bytes of random reads of read_bytes
+ * (512, 1024, 2048 or 4096, at most one cache line) from the start of cache
+ * lines of the bound backing store, eight 16-byte loads in flight per lane as
+ * in the gather; returns the best of three launches in GB/s. Small random
+ * host reads reach less than a bulk copy; this is their ceiling. */
+GIDS_API int gids_store_host_read_gbs(gids_store_t *s, uint32_t read_bytes, uint64_t total_bytes, double *out);
 
 /* -------------------------------------------------------------- gathers --
  * gids_read_feature replaces BAM_Feature_Store<T>::read_feature

@@ -78,6 +78,7 @@ def lib():
             "gids_store_open_peers": (i32, [vp, vp, i32]),
             "gids_store_share_shards": (i32, [P(vp), i32]),
             "gids_store_peer_copy_gbs": (i32, [vp, i32, u64, P(ctypes.c_double)]),
+            "gids_store_host_read_gbs": (i32, [vp, u32, u64, P(ctypes.c_double)]),
             "gids_sampler_create": (i32, [P(vp), i32, vp, vp, i32, u64, P(i32), i32, u64, u64]),
             "gids_sampler_capacity": (i32, [vp, P(u64)]),
             "gids_sampler_sample": (i32, [vp, vp, u64, vp, u64, vp, P(u64), i64, vp]),

@@ -428,3 +428,17 @@ def test_rewrite_invalidates_cache():
     check(rc)
     assert bits_equal(out, oracle.gather(b, ids))
     s.close()
+
+
+def test_host_read_probe(built):
+    """The host-link probe reads random lines of the backing store and rejects
+    read sizes it cannot issue."""
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 61, 20000, 128)  # 512-byte rows
+    s = make_store(t, num_ssd=2, cache_line=512)
+    L = gids_abi.lib()
+    v = ctypes.c_double()
+    check(L.gids_store_host_read_gbs(s.s, 512, 64 << 20, ctypes.byref(v)))
+    assert v.value > 0.5
+    assert L.gids_store_host_read_gbs(s.s, 1024, 1 << 20, ctypes.byref(v)) == gids_abi.GIDS_E_INVAL  # > line
+    assert L.gids_store_host_read_gbs(s.s, 768, 1 << 20, ctypes.byref(v)) == gids_abi.GIDS_E_INVAL
+    s.close()
