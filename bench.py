@@ -306,7 +306,8 @@ PHASES = ("ns_lookup", "ns_fill_wait", "ns_copy", "ns_release")
 CACHE_WARMUP_CACHES = 12
 
 # cache replacement policies: (admission on the second miss, clock counter ceiling)
-POLICIES = {"admit2": (True, 3), "clock": (False, 1), "admit2_sc": (True, 1), "clock3": (False, 3)}
+POLICIES = {"admit2": (True, 3), "clock": (False, 1), "admit2_sc": (True, 1), "clock3": (False, 3),
+            "static": ("static", 3)}
 
 
 def host_link_peak_gbs(device, dist=None) -> float:
@@ -572,6 +573,7 @@ def run_ours(args, cfg, dist: Dist):
         g.BAM_FS.fill_synthetic(KIND[dt], 1, 0)
         t_fill = time.time() - t0
     geo = g.BAM_FS.geometry()
+    line = geo.get("cache_line", page)
     log(f"[rank {dist.rank}] store ready: {geo} (alloc {t_store:.1f}s, fill {t_fill:.1f}s)")
 
     wb = cfg["wb"]
@@ -593,6 +595,26 @@ def run_ours(args, cfg, dist: Dist):
         g.set_cpu_buffer(pins, int(pins.numel()))
         log(f"[rank {dist.rank}] constant CPU buffer: {pins.numel()} pinned rows (PageRank top "
             f"{cfg['cpu_pin_frac']:.0%})")
+    n_static = 0
+    t_static = 0.0
+    if args.policy == "static":
+        # the static hot set: the rows neighbour sampling reaches most often (highest out-degree), as many
+        # as the cache's lines hold (every rank's shard when sharded), pinned and filled in once
+        if cfg["hetero"]:
+            raise SystemExit("the static policy needs a homogeneous graph's CSC")
+        from GIDS.sampler import hot_rows
+
+        t0 = time.time()
+        lpr = -(-row_bytes // line) + (0 if row_bytes % line == 0 else 1)
+        k = geo["cache_slots"] * g.world // lpr
+        _, indices = graph_csc(cfg, device)
+        hot = hot_rows(indices, cfg["nodes"], k)
+        g.pin_cache(hot)
+        n_static = int(hot.numel())
+        del hot
+        torch.cuda.synchronize()
+        t_static = time.time() - t0
+        log(f"[rank {dist.rank}] static hot set: {n_static} rows of highest out-degree pinned in {t_static:.1f}s")
     host_batches = [pin(b) for b in batches]
     stream = torch.cuda.current_stream(device)
     bam = g.BAM_FS
@@ -603,7 +625,6 @@ def run_ours(args, cfg, dist: Dist):
     # timed steps see the page cache of a job that has been training for a while
     # (admission fills the cache with lines that recur, which takes several
     # cache-sizes of line references); then the W warm-up steps
-    line = geo.get("cache_line", page)
     refs_per_batch = float(np.mean(sizes)) * -(-row_bytes // line)
     n_cw = args.cache_warmup
     if n_cw < 0:
@@ -813,6 +834,7 @@ def run_ours(args, cfg, dist: Dist):
                      "constant_cpu_buffer_rows": int(pins.numel()) if pins is not None else 0,
                      "window_buffer_depth": wb,
                      "cache_policy": args.policy,
+                     "static_hot_rows": n_static or None,
                      "cache_warmup_minibatches": n_cw,
                      "gather_grid_cap": args.gather_blocks or None},
         "parity": {"rows_checked": int(dist.sum(sum(p["rows_checked"] for p in parity))),
@@ -831,6 +853,7 @@ def run_ours(args, cfg, dist: Dist):
         "gpu_launches": int(launches) + (len(dev_ids) if wb else 0),
         "clocks": clk,
         "setup_s": {"store": round(t_store, 1), "fill": round(t_fill, 1), "sampling": round(t_sample, 1),
+                    "static_hot_set": round(t_static, 1),
                     "cache_warmup": round(t_cw, 1)},
     }
     torch.cuda.synchronize()
@@ -939,7 +962,8 @@ def main():
                     help="draw minibatches with the torch sampler instead of the CUDA sampler (same ids)")
     ap.add_argument("--policy", default="admit2", choices=sorted(POLICIES),
                     help="cache replacement: admit2 = insert on the second miss + 2-bit clock; clock = insert "
-                         "every miss + second-chance clock (the reference's insertion rule)")
+                         "every miss + second-chance clock (the reference's insertion rule); static = the cache "
+                         "holds the rows of highest out-degree, pinned, and reads every other row through")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3")

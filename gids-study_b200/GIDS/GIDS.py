@@ -46,6 +46,15 @@ def _feature_store_module():
     return BAM_Feature_Store
 
 
+def _admission_mode(v) -> int:
+    """cache_admission -> the store's admission mode (0 every miss, 1 second miss, 2 pinned rows only)."""
+    if isinstance(v, str):
+        if v != "static":
+            raise ValueError(f"cache_admission must be True, False or 'static', not {v!r}")
+        return 2
+    return 1 if v else 0
+
+
 def _current_stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -83,6 +92,10 @@ class GIDS:
     page do not pull whole pages over the host link. ``cache_admission``
     (default True) inserts a line on its second miss within a window of twice
     the cache's slots, so lines touched once do not evict lines touched often;
+    False inserts every miss (the reference's rule); ``"static"`` makes the
+    cache hold only the rows pinned with ``pin_cache`` (a hot set chosen from
+    the graph, for example by ``GIDS.sampler.hot_rows``) and read every other
+    row through;
     ``cache_ref_max`` (default 3) is the clock counter ceiling (1 = the
     second-chance clock). Neither changes what is gathered. ``gather_blocks``
     caps the gather kernel's grid (0: every block the GPU holds at once), so a
@@ -154,7 +167,7 @@ class GIDS:
         if self.world > 1:
             self._attach_peer_shards()
         self.BAM_FS.set_row_layout(cache_dim)
-        self.BAM_FS.set_cache_policy(bool(cache_admission), int(cache_ref_max))
+        self.BAM_FS.set_cache_policy(_admission_mode(cache_admission), int(cache_ref_max))
         if gather_blocks:
             self.BAM_FS.set_gather_blocks(int(gather_blocks))
         self.BAM_FS.set_synchronous(bool(synchronous))
@@ -260,6 +273,34 @@ class GIDS:
         if self.heterograph:
             return [(self._key_off(k), v) for k, v in batch[0].items()]
         return [(0, batch[0])]
+
+    # ---------------------------------------------------------- static hot set
+    def pin_cache(self, node_ids, key=None, prefill=True, chunk_rows=1 << 18):
+        """Pin the GPU-cache lines of rows ``node_ids`` (of node type ``key`` in
+        a heterograph) for good (extension): they are inserted on their first
+        miss and never evicted; with ``cache_admission="static"`` they are the
+        only rows the cache holds. ``prefill`` gathers them once so that they
+        are resident before the next minibatch. Pin at most as many lines as
+        the cache has slots; ``flush_cache`` drops the pins."""
+        ids = _as_index(node_ids, self.device)
+        key_off = self._key_off(key) if key is not None else 0
+        stream = _current_stream_handle(self.device)
+        self.BAM_FS.pin_rows(ids.data_ptr(), len(ids), key_off, stream)
+        if prefill and len(ids):
+            n = min(chunk_rows, len(ids))
+            scratch = torch.empty((n, self.cache_dim), dtype=self.dtype, device=self.device)
+            for lo in range(0, len(ids), chunk_rows):
+                part = ids[lo:lo + chunk_rows]
+                self.BAM_FS.read_feature(scratch.data_ptr(), part.data_ptr(), len(part), self.cache_dim,
+                                         self.cache_dim, key_off, stream)
+            torch.cuda.current_stream(self.device).synchronize()
+            del scratch
+
+    def unpin_cache(self, node_ids, key=None):
+        """Clear the permanent pins of rows ``node_ids`` (extension)."""
+        ids = _as_index(node_ids, self.device)
+        key_off = self._key_off(key) if key is not None else 0
+        self.BAM_FS.unpin_rows(ids.data_ptr(), len(ids), key_off, _current_stream_handle(self.device))
 
     # ----------------------------------------------- storage access accumulator
     def set_required_storage_access(self, bw, l_ssd, l_system, num_ssd, p):

@@ -11,7 +11,12 @@ fetch_feature gathers and of the constant CPU buffer's pin list.
   evaluation/page_rank_node_list_gen.py:126-134, 282-285, in float32 on the
   GPU (the reference's dtype), producing the ``pin_file`` node list.
 
-Both run in the library behind ``BAM_Feature_Store`` (imported on first use).
+* ``out_degree`` / ``hot_rows`` rank nodes by how often neighbour sampling can
+  reach them (their out-degree: the in-edges they are the source of), the
+  rank of a static GPU-cache hot set (``GIDS.pin_cache`` with
+  ``cache_admission="static"``), as degree-ranked GPU feature caches do.
+
+All run in the library behind ``BAM_Feature_Store`` (imported on first use).
 """
 from __future__ import annotations
 
@@ -90,3 +95,23 @@ def pagerank_pin_list(indptr: torch.Tensor, indices: torch.Tensor, fraction: flo
     # the keys are distinct and nonnegative: their k smallest are one order
     top = torch.topk(keys, k, largest=False, sorted=True).values
     return top & 0xFFFFFFFF
+
+
+def out_degree(indices: torch.Tensor, num_nodes: int) -> torch.Tensor:
+    """int32 [num_nodes]: how many in-edges of the CSC graph each node is the source of."""
+    if not indices.is_cuda or indices.dtype not in (torch.int32, torch.int64) or not indices.is_contiguous():
+        raise ValueError("indices must be a contiguous int32 or int64 CUDA tensor")
+    counts = torch.empty(num_nodes, dtype=torch.int32, device=indices.device)
+    stream = torch.cuda.current_stream(indices.device).cuda_stream
+    _store_module().out_degree(indices.device.index, indices.data_ptr(), indices.element_size(), indices.numel(),
+                               num_nodes, counts.data_ptr(), stream)
+    return counts
+
+
+def hot_rows(indices: torch.Tensor, num_nodes: int, k: int) -> torch.Tensor:
+    """The k nodes of highest out-degree, degree descending then node id
+    ascending (int64, on the graph's device)."""
+    counts = out_degree(indices, num_nodes).to(torch.int64)
+    keys = ((0xFFFFFFFF - counts) << 32) | torch.arange(num_nodes, device=indices.device)
+    k = max(0, min(int(k), num_nodes))
+    return torch.topk(keys, k, largest=False, sorted=True).values & 0xFFFFFFFF

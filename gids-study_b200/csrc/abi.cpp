@@ -212,7 +212,7 @@ int gids_store_set_wait_limit(gids_store_t* s, uint32_t polls) {
 int gids_store_set_cache_policy(gids_store_t* s, int admission, uint32_t ref_max) {
   return guarded([&] {
     NEED(s);
-    s->s.set_policy(admission != 0, ref_max);
+    s->s.set_policy(admission, ref_max);
   });
 }
 
@@ -332,7 +332,23 @@ int gids_unset_window_buffering(gids_store_t* s, const int64_t* idx, int64_t n, 
                                 uint32_t row_stride_elems, void* stream) {
   return guarded([&] {
     NEED(s);
-    s->s.window_buffering(idx, n, hash_off, row_stride_elems, (cudaStream_t)stream, true);
+    s->s.window_buffering(idx, n, hash_off, row_stride_elems, (cudaStream_t)stream, gids::WB_UNMARK);
+  });
+}
+
+int gids_store_pin_rows(gids_store_t* s, const int64_t* idx, int64_t n, int64_t hash_off, uint32_t row_stride_elems,
+                        void* stream) {
+  return guarded([&] {
+    NEED(s);
+    s->s.window_buffering(idx, n, hash_off, row_stride_elems, (cudaStream_t)stream, gids::WB_PIN);
+  });
+}
+
+int gids_store_unpin_rows(gids_store_t* s, const int64_t* idx, int64_t n, int64_t hash_off,
+                          uint32_t row_stride_elems, void* stream) {
+  return guarded([&] {
+    NEED(s);
+    s->s.window_buffering(idx, n, hash_off, row_stride_elems, (cudaStream_t)stream, gids::WB_UNPIN);
   });
 }
 
@@ -510,6 +526,13 @@ int gids_pagerank(int device, const int64_t* indptr, const void* indices, int in
   return guarded([&] {
     gids::pagerank(device, indptr, indices, index_bytes, num_nodes, iters, damping, pv, order_keys,
                    (cudaStream_t)stream);
+  });
+}
+
+int gids_out_degree(int device, const void* indices, int index_bytes, uint64_t num_edges, uint64_t num_nodes,
+                    uint32_t* counts, void* stream) {
+  return guarded([&] {
+    gids::out_degree(device, indices, index_bytes, num_edges, num_nodes, counts, (cudaStream_t)stream);
   });
 }
 

@@ -132,6 +132,13 @@ class FeatureStore {
   void unset_window_buffering(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
     check(gids_unset_window_buffering(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
   }
+  // extension: permanent pins of the rows' cache lines (a static hot set)
+  void pin_rows(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
+    check(gids_store_pin_rows(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
+  }
+  void unpin_rows(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
+    check(gids_store_unpin_rows(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
+  }
   // cpu_backing_buffer (gids_nvme.cu:123-139)
   void cpu_backing_buffer(uint64_t dim, uint64_t len) { check(gids_cpu_backing_buffer(s(), dim, len)); }
   // set_cpu_buffer (gids_nvme.cu:694-711)
@@ -191,7 +198,7 @@ class FeatureStore {
     line_ = bytes;
   }
   // replacement policy: admission on the second miss, clock counter ceiling
-  void set_cache_policy(bool admission, uint32_t ref_max) { check(gids_store_set_cache_policy(s(), admission ? 1 : 0, ref_max)); }
+  void set_cache_policy(int admission, uint32_t ref_max) { check(gids_store_set_cache_policy(s(), admission, ref_max)); }
   // cap on the gather's grid (0: every resident block)
   void set_gather_blocks(uint32_t n) { check(gids_store_set_gather_blocks(s(), n)); }
   // NVLink bandwidth: a timed copy from a peer rank's shard (GB/s)
@@ -309,6 +316,10 @@ void bind_store(py::module_& m, const char* name) {
            py::arg("hash_off") = 0, py::arg("stream") = 0, R())
       .def("unset_window_buffering", &S::unset_window_buffering, py::arg("id_idx"), py::arg("num_pages"),
            py::arg("hash_off") = 0, py::arg("stream") = 0, R())
+      .def("pin_rows", &S::pin_rows, py::arg("id_idx"), py::arg("num"), py::arg("hash_off") = 0,
+           py::arg("stream") = 0, R())
+      .def("unpin_rows", &S::unpin_rows, py::arg("id_idx"), py::arg("num"), py::arg("hash_off") = 0,
+           py::arg("stream") = 0, R())
       .def("cpu_backing_buffer", &S::cpu_backing_buffer, py::arg("dim"), py::arg("len"), R())
       .def("set_cpu_buffer", &S::set_cpu_buffer, py::arg("idx_buffer"), py::arg("num"), R())
       .def("flush_cache", &S::flush_cache, R())
@@ -409,6 +420,16 @@ PYBIND11_MODULE(BAM_Feature_Store, m) {
       .def("sample", &Sampler::sample, py::arg("seeds"), py::arg("n_seeds"), py::arg("out"), py::arg("out_cap"),
            py::arg("count_dev") = 0, py::arg("call") = -1, py::arg("stream") = 0,
            py::call_guard<py::gil_scoped_release>());
+  // extension: out-degree histogram of a CSC graph (gids_out_degree)
+  m.def(
+      "out_degree",
+      [](int device, uint64_t indices, int index_bytes, uint64_t num_edges, uint64_t num_nodes, uint64_t counts,
+         uint64_t stream) {
+        check(gids_out_degree(device, (const void*)indices, index_bytes, num_edges, num_nodes, (uint32_t*)counts,
+                              (void*)stream));
+      },
+      py::arg("device"), py::arg("indices"), py::arg("index_bytes"), py::arg("num_edges"), py::arg("num_nodes"),
+      py::arg("counts"), py::arg("stream") = 0, py::call_guard<py::gil_scoped_release>());
   // extension: compute_pagerank of the pin-list generator in float32 (gids_pagerank)
   m.def(
       "pagerank",

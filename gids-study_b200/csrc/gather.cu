@@ -425,15 +425,17 @@ __device__ __forceinline__ const char* backing_addr(const DevBacking& b, uint64_
   return b.ssd[c] + (dp << b.page_shift) + ((l & ((1ull << b.lpp_shift) - 1ull)) << line_shift);
 }
 
-// Saturating decrement of a window-buffer pin counter. The CAS loop runs until
-// it lands or the counter reads 0: every failed CAS means another thread
-// changed the counter, so the loop is bounded by the contention on this one
-// word, and no pin is left behind when it is contended.
+// Saturating decrement of the window-buffer part of a line's pin word (the
+// permanent-pin bit is kept). The CAS loop runs until it lands or the count
+// reads 0: every failed CAS means another thread changed the word, so the
+// loop is bounded by the contention on this one word, and no pin is left
+// behind when it is contended.
 template <bool SYS>
 __device__ __forceinline__ void wb_consume(unsigned int* w, unsigned int cnt) {
   unsigned int v = ld_relaxed_u32<SYS>(w);
-  while (v != 0) {
-    const unsigned int nv = v > cnt ? v - cnt : 0u;
+  while (v & WB_COUNT_MASK) {
+    const unsigned int c = v & WB_COUNT_MASK;
+    const unsigned int nv = (v & WB_PERMANENT) | (c > cnt ? c - cnt : 0u);
     const unsigned int r = atom_cas_u32<SYS>(w, v, nv);
     if (r == v) break;
     v = r;
@@ -585,8 +587,13 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
           // window, read the line straight from the backing store
           // (a line that window buffering has pinned for later batches is
           // admitted at once)
+          // (a line with a permanent pin counts as pinned for good). With the
+          // pinned-only policy the cache holds the permanently pinned lines
+          // alone and every other line is read through.
           bool admit = true;
-          if (gate_sh[owner] && !(S.wb && ld_relaxed_u32<SYS>(S.wb + lp) > cnt)) {
+          if (a.c.pinned_only) {
+            admit = S.wb && (ld_relaxed_u32<SYS>(S.wb + lp) & WB_PERMANENT) != 0u;
+          } else if (gate_sh[owner] && !(S.wb && ld_relaxed_u32<SYS>(S.wb + lp) > cnt)) {
             const unsigned long long bit = 1ull << (lp & 63);
             admit = (atom_or_relaxed<SYS>(S.seen + (lp >> 6), bit) & bit) != 0;
           }
@@ -947,8 +954,9 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
 
 // Window buffering: one thread per node id, +1 on the pin counter of every
 // page its row touches, in the shard that owns the page (gids_kernel.cu:246-256
-// marks one page per id). With a.release, -1 instead (saturating at 0): the
-// marks of a window that will not be gathered are taken back.
+// marks one page per id). WB_UNMARK: -1 instead (saturating at 0), the marks
+// of a window that will not be gathered are taken back. WB_PIN / WB_UNPIN:
+// set / clear the permanent-pin bit of those pages.
 __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.n) return;
@@ -958,17 +966,32 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   const uint64_t b0 = (uint64_t)rs * a.stride;
   const uint64_t p0 = b0 >> a.page_shift, p1 = (b0 + a.row_bytes - 1) >> a.page_shift;
   for (uint64_t p = p0; p <= p1; p++) {
-    if (a.world == 1) {
-      if (a.release)
-        wb_consume<false>(a.wb[0] + p, 1u);
-      else
-        atomicAdd(a.wb[0] + p, 1u);
-    } else {
-      unsigned int* const w = a.wb[p % a.world] + p / a.world;
-      if (a.release)
-        wb_consume<true>(w, 1u);
-      else
-        atomicAdd_system(w, 1u);
+    unsigned int* const w = a.world == 1 ? a.wb[0] + p : a.wb[p % a.world] + p / a.world;
+    switch (a.mode) {
+      case WB_MARK:
+        if (a.world == 1)
+          atomicAdd(w, 1u);
+        else
+          atomicAdd_system(w, 1u);
+        break;
+      case WB_UNMARK:
+        if (a.world == 1)
+          wb_consume<false>(w, 1u);
+        else
+          wb_consume<true>(w, 1u);
+        break;
+      case WB_PIN:
+        if (a.world == 1)
+          atomicOr(w, WB_PERMANENT);
+        else
+          atomicOr_system(w, WB_PERMANENT);
+        break;
+      default:
+        if (a.world == 1)
+          atomicAnd(w, ~WB_PERMANENT);
+        else
+          atomicAnd_system(w, ~WB_PERMANENT);
+        break;
     }
   }
 }

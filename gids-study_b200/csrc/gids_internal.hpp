@@ -65,6 +65,13 @@ constexpr uint64_t ST_VALID = 1ull << 25;
 constexpr int ST_SLOT_SHIFT = 32;
 constexpr uint64_t SLOT_EMPTY = ~0ull;
 
+// Pin word of a line (DevShard::wb): the low 31 bits count window-buffer
+// marks (batches queued to gather the line), the top bit is a permanent pin
+// (gids_store_pin_rows). A line with a nonzero word is never evicted.
+constexpr unsigned int WB_PERMANENT = 0x80000000u;
+constexpr unsigned int WB_COUNT_MASK = 0x7FFFFFFFu;
+enum : uint32_t { WB_MARK = 0, WB_UNMARK = 1, WB_PIN = 2, WB_UNPIN = 3 };
+
 // Per-segment source classes used by the gather kernel and its counters.
 enum : int { CLS_NONE = 0, CLS_HIT = 1, CLS_OWN = 2, CLS_WAIT = 3, CLS_WAITED = 4, CLS_BYPASS = 5 };
 
@@ -77,7 +84,7 @@ struct DevShard {
   unsigned long long* state;      // [n_pages_local] page table
   unsigned long long* slot_page;  // [n_slots] local page index held by each slot (SLOT_EMPTY if none)
   unsigned char* slot_ref;        // [n_slots] clock counter (chances left before eviction)
-  unsigned int* wb;               // [n_pages_local] window-buffer pins, or nullptr
+  unsigned int* wb;               // [n_pages_local] pin words (window marks + permanent bit), or nullptr
   char* slots;                    // [n_slots * page_size] resident pages
   unsigned long long* clock;      // clock hand
   unsigned long long* seen;       // [n_pages_local / 64 + 1] admission bits, or nullptr (admit every miss)
@@ -96,6 +103,7 @@ struct DevCache {
   uint32_t world;  // ranks sharing the cache (1 = unsharded)
   uint32_t rank;
   uint32_t ref_max;  // clock counter ceiling: 1 = second chance, >1 = frequency clock
+  uint32_t pinned_only;  // 1: only permanently pinned lines are inserted; the rest read through
 };
 
 struct DevBacking {
@@ -153,7 +161,7 @@ struct WbArgs {
   uint64_t row_bytes;
   uint64_t n_rows;
   uint32_t page_shift;
-  uint32_t release;  // 0: add one pin per (row, page); 1: take one back (saturating)
+  uint32_t mode;  // WB_MARK, WB_UNMARK, WB_PIN or WB_UNPIN, per (row, page)
 };
 
 // Launchers (gather.cu). sys = the cache is shared with other GPUs, so
@@ -175,6 +183,8 @@ void sampler_sample(Sampler* s, const int64_t* seeds, uint64_t n_seeds, int64_t*
                     uint64_t* count_dev, uint64_t* host_count, int64_t call, cudaStream_t st);
 void pagerank(int device, const int64_t* indptr, const void* indices, int index_bytes, uint64_t n, int iters,
               double damping, float* pv, uint64_t* keys, cudaStream_t st);
+void out_degree(int device, const void* indices, int index_bytes, uint64_t n_edges, uint64_t n, uint32_t* counts,
+                cudaStream_t st);
 
 // ------------------------------------------------------- emulated SSDs
 struct SsdRegion {
@@ -238,10 +248,11 @@ class Store {
                         uint64_t num_ele, uint64_t num_ssd);
   void read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
                   int cache_dim, const uint64_t* key_offs, cudaStream_t st);
-  // release = false: mark the rows' lines (one pin per row and line);
-  // release = true: take those marks back (a window that will not be gathered)
+  // mode WB_MARK: mark the rows' lines (one pin per row and line); WB_UNMARK:
+  // take those marks back (a window that will not be gathered); WB_PIN /
+  // WB_UNPIN: set / clear the lines' permanent pins
   void window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st,
-                        bool release = false);
+                        uint32_t mode = WB_MARK);
   void clear_window_pins();
   void cpu_backing_buffer(uint64_t dim, uint64_t len);
   void set_cpu_buffer(const int64_t* host_idx, int64_t num);
@@ -251,10 +262,10 @@ class Store {
   uint32_t wait_limit = 1u << 16;  // polls of a BUSY line before giving up and bypassing
   // replacement policy: admission (a line is inserted on its second miss
   // within a window of 2 x n_slots line references) and clock counter ceiling
-  bool admission = true;
+  int admission = 1;  // 0: insert every miss, 1: insert on the second miss, 2: pinned lines only
   uint32_t ref_max = 3;
   uint64_t refs_since_seen_reset = 0;
-  void set_policy(bool admit, uint32_t ref_ceiling);
+  void set_policy(int admit, uint32_t ref_ceiling);
   void set_gather_blocks(uint32_t n);
   // gather with the page cache in the library's static no-allocation scratch (noalloc.cu)
   void read_noalloc(void* out, const int64_t* idx, int64_t n, int dim, int cache_dim, uint64_t key_off,

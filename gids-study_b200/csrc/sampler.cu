@@ -405,6 +405,22 @@ __global__ void pr_key_kernel(const float* __restrict__ pv, unsigned long long n
   }
 }
 
+// out-degree of every node: the number of in-edges it is the source of, i.e.
+// how often neighbour sampling can reach it (the rank of a static hot set)
+__global__ void outdeg_kernel(const void* __restrict__ indices, int index_bytes, unsigned long long n_edges,
+                              unsigned long long n, unsigned int* __restrict__ counts,
+                              unsigned int* __restrict__ bad) {
+  for (unsigned long long e = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; e < n_edges;
+       e += (unsigned long long)gridDim.x * blockDim.x) {
+    const long long v = index_bytes == 4 ? (long long)__ldg(reinterpret_cast<const int*>(indices) + e)
+                                         : __ldg(reinterpret_cast<const long long*>(indices) + e);
+    if (v >= 0 && (unsigned long long)v < n)
+      atomicAdd(counts + v, 1u);
+    else
+      atomicOr(bad, 1u);
+  }
+}
+
 int grid_for(int dev, unsigned long long work, int per_block) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -571,6 +587,28 @@ void pagerank(int device, const int64_t* indptr, const void* indices, int index_
   if (keys) pr_key_kernel<<<ge, SMP_THREADS, 0, st>>>(pv, n, reinterpret_cast<unsigned long long*>(keys));
   GIDS_CUDA(cudaGetLastError());
   GIDS_CUDA(cudaFreeAsync(norm, st));
+}
+
+// Out-degree histogram of a CSC graph's sources into counts[n] (device).
+void out_degree(int device, const void* indices, int index_bytes, uint64_t n_edges, uint64_t n, uint32_t* counts,
+                cudaStream_t st) {
+  GIDS_CHECK(counts && (indices || n_edges == 0), GIDS_E_INVAL, "null array");
+  GIDS_CHECK(index_bytes == 4 || index_bytes == 8, GIDS_E_INVAL, "index_bytes must be 4 or 8");
+  GIDS_CHECK(n > 0, GIDS_E_INVAL, "node count must be > 0");
+  DeviceGuard dg(device);
+  unsigned int* bad = nullptr;
+  GIDS_CUDA(cudaMallocAsync(&bad, sizeof(unsigned int), st));
+  GIDS_CUDA(cudaMemsetAsync(bad, 0, sizeof(unsigned int), st));
+  GIDS_CUDA(cudaMemsetAsync(counts, 0, n * sizeof(uint32_t), st));
+  if (n_edges)
+    outdeg_kernel<<<grid_for(device, n_edges, SMP_THREADS), SMP_THREADS, 0, st>>>(indices, index_bytes, n_edges, n,
+                                                                                  counts, bad);
+  GIDS_CUDA(cudaGetLastError());
+  unsigned int h = 0;
+  GIDS_CUDA(cudaMemcpyAsync(&h, bad, sizeof(h), cudaMemcpyDeviceToHost, st));
+  GIDS_CUDA(cudaFreeAsync(bad, st));
+  GIDS_CUDA(cudaStreamSynchronize(st));
+  GIDS_CHECK(h == 0, GIDS_E_RANGE, "an edge of the CSC graph has a source outside the graph");
 }
 
 }  // namespace gids

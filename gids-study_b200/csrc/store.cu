@@ -256,7 +256,8 @@ DevCache Store::dev_cache() const {
   c.world = world;
   c.rank = rank;
   c.ref_max = ref_max;
-  if (!admission)
+  c.pinned_only = admission == 2 ? 1u : 0u;
+  if (admission != 1)
     for (uint32_t r = 0; r < world; r++) c.sh[r].seen = nullptr;
   return c;
 }
@@ -323,9 +324,10 @@ void Store::debug_mark_busy(uint64_t line) {
   GIDS_CUDA(cudaMemcpy(d_state + (world == 1 ? line : line / world), &busy, sizeof(busy), cudaMemcpyHostToDevice));
 }
 
-void Store::set_policy(bool admit, uint32_t ref_ceiling) {
+void Store::set_policy(int admit, uint32_t ref_ceiling) {
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(ref_ceiling >= 1 && ref_ceiling <= 255, GIDS_E_INVAL, "clock counter ceiling must be in [1, 255]");
+  GIDS_CHECK(admit >= 0 && admit <= 2, GIDS_E_INVAL, "admission must be 0, 1 or 2");
   admission = admit;
   ref_max = ref_ceiling;
 }
@@ -406,7 +408,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
   a.spin_limit = wait_limit;
   a.sweep_limit = 64;
   uint64_t rows_total = 0;
-  if (admission && n_slots) {
+  if (admission == 1 && n_slots) {
     // age the admission bits: clear this shard's after 2 x n_slots line references
     uint64_t refs = 0;
     for (int i = 0; i < k; i++) refs += ns[i] * max_pages;
@@ -469,9 +471,9 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
 }
 
 void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_t stride_elems, cudaStream_t st,
-                             bool release) {
+                             uint32_t mode) {
   std::lock_guard<std::mutex> lk(mu);
-  NvtxRange nv(release ? "gids.window_unmark" : "gids.window_buffering");
+  NvtxRange nv(mode == WB_MARK ? "gids.window_buffering" : mode == WB_UNMARK ? "gids.window_unmark" : "gids.pin");
   GIDS_CHECK(initialized, GIDS_E_STATE, "set_window_buffering before init_controllers");
   GIDS_CHECK(n >= 0, GIDS_E_INVAL, "n must be >= 0");
   if (n == 0) return;
@@ -479,7 +481,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   DeviceGuard g(device);
   if (!d_wb) {
-    if (release) return;  // nothing was ever marked
+    if (mode == WB_UNMARK || mode == WB_UNPIN) return;  // nothing was ever marked
     GIDS_CUDA(cudaMalloc(&d_wb, n_lines * sizeof(unsigned int)));
     GIDS_CUDA(cudaMemset(d_wb, 0, n_lines * sizeof(unsigned int)));
   }
@@ -496,7 +498,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   w.row_bytes = w.stride;
   w.n_rows = range_bytes >= w.row_bytes ? (range_bytes - w.row_bytes) / w.stride + 1 : 0;
   w.page_shift = line_shift;
-  w.release = release ? 1u : 0u;
+  w.mode = mode;
   launch_wb_mark(w, st);
   last_stream = st;
   if (synchronous) GIDS_CUDA(cudaStreamSynchronize(st));

@@ -123,9 +123,14 @@ GIDS_API int gids_store_set_cache_line(gids_store_t *s, uint32_t bytes);
  * page_cache_backup.h:2107-2256). admission = 1 (default): a line is inserted
  * on its second miss within a window of 2 x (cache slots) line references;
  * its first miss reads the backing store directly, so lines touched once do
- * not evict lines touched often. ref_max (default 3): a hit adds a chance up
- * to ref_max and the clock hand spends one per pass (1 = second chance).
- * Results do not depend on the policy; only hit ratios do. */
+ * not evict lines touched often. admission = 0: every miss is inserted (the
+ * reference's rule). admission = 2 (static cache): only lines with a
+ * permanent pin (gids_store_pin_rows) are inserted, on their first reference,
+ * and every other line is read through -- a cache that holds a chosen hot set
+ * (for example the rows of highest out-degree, gids_out_degree). ref_max
+ * (default 3): a hit adds a chance up to ref_max and the clock hand spends one
+ * per pass (1 = second chance). Results do not depend on the policy; only hit
+ * ratios do. */
 GIDS_API int gids_store_set_cache_policy(gids_store_t *s, int admission, uint32_t ref_max);
 /* Largest grid of one gather launch, in blocks of 256 threads (no reference
  * counterpart). 0 (default): every block the GPU can hold at once (2 per SM).
@@ -239,6 +244,19 @@ GIDS_API int gids_set_window_buffering(gids_store_t *s, const int64_t *idx, int6
  * every pin of the calling rank's shard. */
 GIDS_API int gids_unset_window_buffering(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
                                          uint32_t row_stride_elems, void *stream);
+/* Permanent pins (no reference counterpart; the reference keeps its hot set
+ * in the constant CPU buffer instead, gids_cpu_backing_buffer): the cache
+ * lines of rows (idx[i] + hash_off) (device int64 array; rows map to lines by
+ * bytes as above) are never evicted once resident and are inserted on their
+ * first miss whatever the admission rule; with admission = 2 they are the only
+ * lines the cache holds. Pin at most as many lines as the cache has slots
+ * (with a sharded cache, per owning shard); lines beyond that are read
+ * through. unpin clears the pins; flush_cache clears every pin of the shard.
+ * Gathering the pinned rows once fills them in. */
+GIDS_API int gids_store_pin_rows(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
+                                 uint32_t row_stride_elems, void *stream);
+GIDS_API int gids_store_unpin_rows(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
+                                   uint32_t row_stride_elems, void *stream);
 
 /* --------------------------------------------------- constant CPU buffer --
  * cpu_backing_buffer (gids_nvme.cu:123-139): allocate a pinned, GPU-mapped
@@ -372,6 +390,14 @@ GIDS_API int gids_sampler_destroy(gids_sampler_t *s);
  * takes torch.topk of pv). */
 GIDS_API int gids_pagerank(int device, const int64_t *indptr, const void *indices, int index_bytes, uint64_t num_nodes,
                            int iters, double damping, float *pv, uint64_t *order_keys, void *stream);
+
+/* Out-degree of every node of a CSC graph (no reference counterpart; the rank
+ * of a static hot set for gids_store_pin_rows): counts[v] (device uint32
+ * [num_nodes]) = the number of in-edges whose source is v, i.e. how often
+ * neighbour sampling can reach v. Waits for `stream`; a source outside the
+ * graph gives GIDS_E_RANGE. */
+GIDS_API int gids_out_degree(int device, const void *indices, int index_bytes, uint64_t num_edges, uint64_t num_nodes,
+                             uint32_t *counts, void *stream);
 
 #ifdef __cplusplus
 }

@@ -52,6 +52,9 @@ def lib():
             "gids_read_feature_noalloc": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
             "gids_set_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_unset_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
+            "gids_store_pin_rows": (i32, [vp, vp, i64, i64, u32, vp]),
+            "gids_store_unpin_rows": (i32, [vp, vp, i64, i64, u32, vp]),
+            "gids_out_degree": (i32, [i32, vp, i32, u64, u64, vp, vp]),
             "gids_cpu_backing_buffer": (i32, [vp, u64, u64]),
             "gids_set_cpu_buffer": (i32, [vp, vp, i32]),
             "gids_set_cpu_buffer_host": (i32, [vp, vp, i64]),
@@ -173,7 +176,8 @@ class Store:
         check(lib().gids_reset_stats(self.s))
 
     def set_policy(self, admission, ref_max):
-        check(lib().gids_store_set_cache_policy(self.s, 1 if admission else 0, ref_max))
+        mode = (1 if admission else 0) if isinstance(admission, bool) else int(admission)
+        check(lib().gids_store_set_cache_policy(self.s, mode, ref_max))
 
     def geometry(self):
         v = (ctypes.c_uint64 * 7)()

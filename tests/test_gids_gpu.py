@@ -181,3 +181,22 @@ def test_sampler_draws_the_same_minibatches_on_cpu_and_gpu(built):
         out[dev] = [s.sample(b)[0].cpu() for b in seed_batches(g.N, 512, 3, 1000, device=dev)]
     for a, b in zip(out["cpu"], out["cuda"]):
         assert torch.equal(a, b)
+
+
+def test_static_hot_set_through_gids(table):
+    from GIDS.sampler import hot_rows
+
+    g = make_gids(table, cache_admission="static")  # 1 MB cache: 256 lines of 4 KB = 1024 rows
+    rng = np.random.default_rng(12)
+    src = torch.as_tensor(rng.zipf(1.2, size=100000) % ROWS).cuda()  # sources of some graph's edges
+    hot = hot_rows(src, ROWS, 1000)
+    g.pin_cache(hot)
+    st0 = g.get_stats()
+    bs = homo_batches(3, 3000, 13)
+    check_homo(table, run(g, bs, 3, CDIM), bs, CDIM)
+    st = g.get_stats()
+    hits = st["hit"] - st0["hit"]
+    hot_set = set(hot.cpu().numpy().tolist())
+    n_hot_refs = sum(int(np.isin(b[0].numpy(), list(hot_set)).sum()) for b in bs)
+    assert st["read_io"] == st0["read_io"] and hits >= n_hot_refs > 0  # nothing new inserted, pinned rows hit
+    g.close()

@@ -168,3 +168,70 @@ def test_flush_cache_drops_window_pins(table):
     st = run(s, table, np.arange(2000, 2256))
     assert (st["evictions"], st["miss"], st["bypass"]) == (256, 256, 0)
     s.close()
+
+
+def _pin(s, ids, unpin=False):
+    L = gids_abi.lib()
+    d = torch.as_tensor(ids, dtype=torch.int64).cuda()
+    f = L.gids_store_unpin_rows if unpin else L.gids_store_pin_rows
+    check(f(s.s, ctypes.c_void_p(d.data_ptr()), len(ids), 0, 0, None))
+    torch.cuda.synchronize()
+
+
+def test_static_policy_holds_only_pinned_lines(table):
+    s = make(table, 1)  # 256 slots
+    s.set_policy(2, 3)
+    hot = np.arange(0, 200)
+    _pin(s, hot)
+    st = run(s, table, hot)
+    assert (st["miss"], st["read_io"], st["bypass"]) == (200, 200, 0)  # inserted on first touch
+    st = run(s, table, np.arange(1000, 1200))
+    assert (st["bypass"], st["miss"], st["evictions"]) == (200, 0, 0)  # unpinned rows read through
+    st = run(s, table, hot[::-1].copy())
+    assert st["hit"] == 200
+    # unpinned lines become evictable again once the policy inserts misses
+    _pin(s, hot[:100], unpin=True)
+    s.set_policy(0, 1)
+    st = run(s, table, np.arange(2000, 2156))  # the 56 free slots, then evictions of the unpinned lines
+    assert st["miss"] == 156 and st["bypass"] == 0 and st["evictions"] == 100
+    assert run(s, table, hot[100:])["hit"] == 100  # still pinned, never evicted
+    s.close()
+
+
+def test_permanent_pins_survive_window_consumption_and_flush_drops_them(table):
+    s = make(table, 1)
+    s.set_policy(0, 1)  # insert every miss: only the pins protect lines
+    hot = np.arange(0, 128)
+    _pin(s, hot)
+    _mark(s, hot, times=2)  # window marks on pinned lines are consumed by gathers, the pin bit stays
+    assert run(s, table, hot)["miss"] == 128
+    run(s, table, hot)
+    for k in range(4):  # churn through the other 128 slots many times over
+        run(s, table, np.arange(1000 + 400 * k, 1400 + 400 * k))
+    assert run(s, table, hot)["hit"] == 128
+    check(gids_abi.lib().gids_flush_cache(s.s))  # drops the lines and every pin
+    assert run(s, table, hot)["miss"] == 128
+    st = run(s, table, np.arange(2000, 2256))
+    assert st["evictions"] > 0
+    s.close()
+
+
+def test_out_degree_and_hot_rows(built):
+    from GIDS.sampler import hot_rows, out_degree
+
+    rng = np.random.default_rng(5)
+    n = 50000
+    for dt in (np.int32, np.int64):
+        ind = rng.zipf(1.3, size=400000) % n
+        ind = ind.astype(dt)
+        d = torch.as_tensor(ind).cuda()
+        got = out_degree(d, n).cpu().numpy()
+        want = np.bincount(ind.astype(np.int64), minlength=n)
+        assert np.array_equal(got, want)
+        top = hot_rows(d, n, 777).cpu().numpy()
+        order = np.lexsort((np.arange(n), -want))
+        assert top.tolist() == order[:777].tolist()
+    L = gids_abi.lib()
+    bad = torch.tensor([1, 2, n + 5], dtype=torch.int64, device="cuda")
+    cnt = torch.empty(n, dtype=torch.int32, device="cuda")
+    assert L.gids_out_degree(0, bad.data_ptr(), 8, 3, n, cnt.data_ptr(), None) == gids_abi.GIDS_E_RANGE
