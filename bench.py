@@ -51,7 +51,10 @@ for _p in (REPO, PKG):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-BASE = dict(cpu_pin_frac=0.0, wb=0, phys_gb=64.0, line=0, hetero=None)
+# policy: the default cache policy of the config (see POLICIES): the homogeneous graphs without window
+# buffering hold a static hot set (the rows of highest out-degree); the heterograph (no CSC here) and the
+# window-buffered config 4 keep the dynamic policy
+BASE = dict(cpu_pin_frac=0.0, wb=0, phys_gb=64.0, line=0, hetero=None, policy="static")
 C3_TYPES = {"t0": 40_000_000, "t1": 30_000_000, "t2": 5_000_000, "t3": 1_000_000}
 C3_RELATIONS = [("t0", "t0"), ("t1", "t0"), ("t2", "t0"), ("t3", "t0"), ("t0", "t1"), ("t1", "t2")]
 CONFIGS = {
@@ -63,10 +66,10 @@ CONFIGS = {
                cache_mb=40 * 1024, fanouts=[15, 10, 5], batch=4096, seed_zipf=None),
     "c3": dict(BASE, nodes=sum(C3_TYPES.values()), mean_deg=8, alpha=1.0, dim=1024, dtype="float32", page=4096,
                ssds=4, cache_mb=40 * 1024, fanouts=[15, 10], batch=1024, seed_zipf=None,
-               hetero=dict(types=C3_TYPES, relations=C3_RELATIONS, seed_type="t0")),
+               hetero=dict(types=C3_TYPES, relations=C3_RELATIONS, seed_type="t0"), policy="admit2"),
     "c4": dict(BASE, nodes=50_000_000, mean_deg=15, alpha=1.2, dim=768, dtype="float16", page=4096, ssds=4,
                cache_mb=8 * 1024, fanouts=[10, 10], batch=2048, seed_zipf=1.0, cpu_pin_frac=0.01, wb=8,
-               phys_gb=80.0, line=512),
+               phys_gb=80.0, line=512, policy="admit2"),
     "c5": dict(BASE, nodes=500_000_000, mean_deg=10, alpha=1.1, dim=128, dtype="float32", page=4096, ssds=8,
                cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None, line=512),
 }
@@ -609,8 +612,10 @@ def run_ours(args, cfg, dist: Dist):
         k = geo["cache_slots"] * g.world // lpr
         _, indices = graph_csc(cfg, device)
         hot = hot_rows(indices, cfg["nodes"], k)
+        if g.world > 1:  # each rank pins and fills the rows whose first line its shard owns
+            hot = hot[((hot * row_bytes) // line) % g.world == g.rank]
         g.pin_cache(hot)
-        n_static = int(hot.numel())
+        n_static = int(dist.sum(hot.numel()))
         del hot
         torch.cuda.synchronize()
         t_static = time.time() - t0
@@ -960,8 +965,9 @@ def main():
                          "enough for about 12 cache-sizes of line references, at most 60")
     ap.add_argument("--torch-sampler", action="store_true",
                     help="draw minibatches with the torch sampler instead of the CUDA sampler (same ids)")
-    ap.add_argument("--policy", default="admit2", choices=sorted(POLICIES),
-                    help="cache replacement: admit2 = insert on the second miss + 2-bit clock; clock = insert "
+    ap.add_argument("--policy", default="", choices=[""] + sorted(POLICIES),
+                    help="cache replacement (default: the config's): admit2 = insert on the second miss + 2-bit "
+                         "clock; clock = insert "
                          "every miss + second-chance clock (the reference's insertion rule); static = the cache "
                          "holds the rows of highest out-degree, pinned, and reads every other row through")
     args = ap.parse_args()
@@ -980,6 +986,8 @@ def main():
     if args.cache_line >= 0:
         cfg["line"] = args.cache_line
     cfg["torch_sampler"] = args.torch_sampler
+    if not args.policy:
+        args.policy = cfg["policy"]
 
     dist = Dist()
     if args.impl == "reference":

@@ -186,10 +186,10 @@ def test_sampler_draws_the_same_minibatches_on_cpu_and_gpu(built):
 def test_static_hot_set_through_gids(table):
     from GIDS.sampler import hot_rows
 
-    g = make_gids(table, cache_admission="static")  # 1 MB cache: 256 lines of 4 KB = 1024 rows
+    g = make_gids(table, cache_admission="static")  # 1 MB cache: 256 lines of 4 KB (4 rows each)
     rng = np.random.default_rng(12)
     src = torch.as_tensor(rng.zipf(1.2, size=100000) % ROWS).cuda()  # sources of some graph's edges
-    hot = hot_rows(src, ROWS, 1000)
+    hot = hot_rows(src, ROWS, 200)  # at most 200 lines: every pinned line gets a slot
     g.pin_cache(hot)
     st0 = g.get_stats()
     bs = homo_batches(3, 3000, 13)
