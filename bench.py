@@ -74,11 +74,11 @@ CONFIGS = {
                cache_mb=20 * 1024, fanouts=[20, 15, 10], batch=8192, seed_zipf=None, line=512),
 }
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per gathered row of gather_kernel, from one
-# ncu --set full capture of a small case of the same config, after the same cache warm-up
-# (config 2: 4M nodes, 2 GB cache, batch 512, 16 warm-up minibatches -> 2.495 GB over 366,578
-# rows at 44 % hits; the full run has 39 %); a full launch's traffic is this times its rows.
-# Configs without such a capture report null.
-TRAFFIC_PER_ROW = {"c2": 2.495e9 / 366578}
+# ncu --set full capture of a small case of the same config and policy, after the same cache warm-up
+# (config 2, static hot set: 4M nodes, 2 GB cache, batch 512 -> 2.467 GB over 366,742 rows at 50 %
+# hits; the full run has 45 %); a full launch's traffic is this times its rows. Other configs and
+# policies report null.
+TRAFFIC_PER_ROW = {("c2", "static"): 2.4666e9 / 366742}
 KIND = {"float32": 1, "float16": 2}
 METRIC = "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs"
 DATA = "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)"
@@ -787,8 +787,8 @@ def run_ours(args, cfg, dist: Dist):
     roofline = {
         "bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": unit_peak,
         "frac": round(t_star / t_launch, 4),
-        "traffic": (int(TRAFFIC_PER_ROW[args.config] * rows_l) if args.config in TRAFFIC_PER_ROW and not args.nodes
-                    and dist.world == 1 else None),
+        "traffic": (int(TRAFFIC_PER_ROW[(args.config, args.policy)] * rows_l)
+                    if (args.config, args.policy) in TRAFFIC_PER_ROW and not args.nodes and dist.world == 1 else None),
         "peak_source": {"hbm": hbm_src + " (of measured)",
                         "host_link": "pinned host->device copy measured live in this run, all ranks copying at "
                                      "once (of measured)",
