@@ -603,18 +603,33 @@ def run_ours(args, cfg, dist: Dist):
     if args.policy == "static":
         # the static hot set: the rows neighbour sampling reaches most often (highest out-degree), as many
         # as the cache's lines hold (every rank's shard when sharded), pinned and filled in once
-        if cfg["hetero"]:
-            raise SystemExit("the static policy needs a homogeneous graph's CSC")
-        from GIDS.sampler import hot_rows
+        from GIDS.sampler import hot_rows, out_degree, top_rows
 
         t0 = time.time()
         lpr = -(-row_bytes // line) + (0 if row_bytes % line == 0 else 1)
         k = geo["cache_slots"] * g.world // lpr
-        _, indices = graph_csc(cfg, device)
-        hot = hot_rows(indices, cfg["nodes"], k)
+        if cfg["hetero"]:
+            # a node's out-degree summed over the relations it is a source of, in global ids
+            # (the types laid out one after another, heterograph_map)
+            from GIDS.synthetic import HeteroSyntheticGraph
+
+            h = cfg["hetero"]
+            hg = HeteroSyntheticGraph(h["types"], h["relations"], cfg["mean_deg"], cfg["alpha"], seed=0,
+                                      device=device)
+            counts = torch.zeros(cfg["nodes"], dtype=torch.int32, device=device)
+            for (src, dst), rg in hg.rel.items():
+                _, ind = rg.materialize(torch.int32, n_dst=h["types"][dst])
+                lo = hmap[src]
+                counts[lo:lo + h["types"][src]] += out_degree(ind, h["types"][src])
+                del ind
+            hot = top_rows(counts, k)
+            del hg, counts
+        else:
+            _, indices = graph_csc(cfg, device)
+            hot = hot_rows(indices, cfg["nodes"], k)
         if g.world > 1:  # each rank pins and fills the rows whose first line its shard owns
             hot = hot[((hot * row_bytes) // line) % g.world == g.rank]
-        g.pin_cache(hot)
+        g.pin_cache(hot)  # global row ids (heterograph: no type offset)
         n_static = int(dist.sum(hot.numel()))
         del hot
         torch.cuda.synchronize()

@@ -108,10 +108,17 @@ def out_degree(indices: torch.Tensor, num_nodes: int) -> torch.Tensor:
     return counts
 
 
+def top_rows(counts: torch.Tensor, k: int) -> torch.Tensor:
+    """The k nodes of largest count (counts < 2^32 per node, fewer than 2^32
+    nodes), count descending then node id ascending (int64)."""
+    n = counts.numel()
+    keys = ((0xFFFFFFFF - counts.to(torch.int64)) << 32) | torch.arange(n, device=counts.device)
+    k = max(0, min(int(k), n))
+    # the keys are distinct and nonnegative: their k smallest are one order
+    return torch.topk(keys, k, largest=False, sorted=True).values & 0xFFFFFFFF
+
+
 def hot_rows(indices: torch.Tensor, num_nodes: int, k: int) -> torch.Tensor:
     """The k nodes of highest out-degree, degree descending then node id
     ascending (int64, on the graph's device)."""
-    counts = out_degree(indices, num_nodes).to(torch.int64)
-    keys = ((0xFFFFFFFF - counts) << 32) | torch.arange(num_nodes, device=indices.device)
-    k = max(0, min(int(k), num_nodes))
-    return torch.topk(keys, k, largest=False, sorted=True).values & 0xFFFFFFFF
+    return top_rows(out_degree(indices, num_nodes), k)

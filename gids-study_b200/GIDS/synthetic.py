@@ -160,17 +160,20 @@ class SyntheticGraph:
         off = torch.minimum(off, (cnt - 1).clamp(min=0))
         return self._order[self._class_off[c] + off]
 
-    def materialize(self, index_dtype=torch.int64, chunk_rows: int = 1 << 22):
-        """Explicit CSC (indptr int64 [N+1], indices [E] of index_dtype) of the
-        graph: indices[indptr[v] + j] = in_neighbor(v, j), built chunk by
-        chunk of destination rows."""
+    def materialize(self, index_dtype=torch.int64, chunk_rows: int = 1 << 22, n_dst: int | None = None):
+        """Explicit CSC (indptr int64 [n_dst+1], indices [E] of index_dtype) of
+        the graph: indices[indptr[v] + j] = in_neighbor(v, j), built chunk by
+        chunk of destination rows. n_dst (default N) is the number of
+        destinations: a heterograph relation's destinations are another node
+        type than its sources."""
         dev = self.device
-        deg = self.in_degree(torch.arange(self.N, device=dev))
-        indptr = torch.zeros(self.N + 1, dtype=torch.int64, device=dev)
+        nd = self.N if n_dst is None else int(n_dst)
+        deg = self.in_degree(torch.arange(nd, device=dev))
+        indptr = torch.zeros(nd + 1, dtype=torch.int64, device=dev)
         torch.cumsum(deg, 0, out=indptr[1:])
         indices = torch.empty(int(indptr[-1]), dtype=index_dtype, device=dev)
-        for lo in range(0, self.N, chunk_rows):
-            hi = min(self.N, lo + chunk_rows)
+        for lo in range(0, nd, chunk_rows):
+            hi = min(nd, lo + chunk_rows)
             d = deg[lo:hi]
             rows = torch.repeat_interleave(torch.arange(lo, hi, device=dev), d)
             j = torch.arange(rows.numel(), device=dev) - torch.repeat_interleave(indptr[lo:hi] - indptr[lo], d)

@@ -113,3 +113,16 @@ def test_chunked_csc_equals_one_chunk():
     ip, ind = g.materialize()
     ip2, ind2 = g.materialize(torch.int32, chunk_rows=7000)
     assert torch.equal(ip, ip2) and ind2.dtype == torch.int32 and torch.equal(ind, ind2.long())
+
+
+def test_relation_csc_has_its_own_destinations():
+    """A heterograph relation's CSC spans the destination type, whose size
+    differs from the source type's."""
+    g = SyntheticGraph(5000, 8, 1.0, seed=3)
+    ip, ind = g.materialize(torch.int32, n_dst=3000, chunk_rows=1000)
+    assert ip.numel() == 3001 and int(ip[-1]) == ind.numel()
+    v = torch.arange(3000)
+    assert torch.equal(ip[1:] - ip[:-1], g.in_degree(v))
+    rows = torch.repeat_interleave(v, ip[1:] - ip[:-1])
+    j = torch.arange(ind.numel()) - torch.repeat_interleave(ip[:-1], ip[1:] - ip[:-1])
+    assert torch.equal(ind.long(), g.in_neighbor(rows, j)) and int(ind.max()) < 5000
