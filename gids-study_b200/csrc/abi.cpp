@@ -482,10 +482,10 @@ int gids_store_geometry(gids_store_t* s, uint64_t* out, int count) {
     NEED(s);
     NEED(out);
     GIDS_CHECK(s->s.initialized, GIDS_E_STATE, "geometry before init_controllers");
-    const uint64_t g[7] = {s->s.n_pages, s->s.ctrls->wrap_pages, s->s.ctrls->ssd.empty() ? 0 : s->s.ctrls->ssd[0].bytes,
+    const uint64_t g[8] = {s->s.n_pages, s->s.ctrls->wrap_pages, s->s.ctrls->ssd.empty() ? 0 : s->s.ctrls->ssd[0].bytes,
                            s->s.n_slots, s->s.page_size,         s->s.ctrls->n_bound,
-                           s->s.line_size};
-    for (int i = 0; i < count && i < 7; i++) out[i] = g[i];
+                           s->s.line_size, s->s.shard_bytes};
+    for (int i = 0; i < count && i < 8; i++) out[i] = g[i];
   });
 }
 

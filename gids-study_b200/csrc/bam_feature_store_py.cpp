@@ -258,8 +258,8 @@ class FeatureStore {
     check(gids_read_range_host(s(), (void*)dst, nbytes, offset));
   }
   py::dict geometry() {
-    uint64_t g[7] = {0};
-    check(gids_store_geometry(s(), g, 7));
+    uint64_t g[8] = {0};
+    check(gids_store_geometry(s(), g, 8));
     py::dict d;
     d["range_pages"] = g[0];
     d["wrap_pages"] = g[1];
@@ -268,6 +268,7 @@ class FeatureStore {
     d["page_size"] = g[4];
     d["num_ssd"] = g[5];
     d["cache_line"] = g[6];
+    d["shard_bytes"] = g[7];
     return d;
   }
   uint32_t elem_bytes() const { return eb_; }

@@ -344,7 +344,9 @@ GIDS_API int gids_read_range_host(gids_store_t *s, void *dst, uint64_t nbytes, u
 GIDS_API int gids_fill_synthetic(gids_store_t *s, int kind, uint64_t seed, int threads);
 /* Geometry of the bound backing store: [0]=pages in the range, [1]=pages
  * physically held (wrap period), [2]=bytes per SSD, [3]=cache slots,
- * [4]=page size, [5]=number of SSDs, [6]=cache line size. */
+ * [4]=page size, [5]=number of SSDs, [6]=cache line size, [7]=bytes of this
+ * store's cache allocation on its GPU (page table, slots and their metadata:
+ * one allocation, a whole number of 2 MB pages). */
 GIDS_API int gids_store_geometry(gids_store_t *s, uint64_t *out, int count);
 
 /* ------------------------------------------------------------- sampler --

@@ -180,7 +180,7 @@ class Store:
         check(lib().gids_store_set_cache_policy(self.s, mode, ref_max))
 
     def geometry(self):
-        v = (ctypes.c_uint64 * 7)()
-        check(lib().gids_store_geometry(self.s, v, 7))
+        v = (ctypes.c_uint64 * 8)()
+        check(lib().gids_store_geometry(self.s, v, 8))
         return dict(zip(["range_pages", "wrap_pages", "ssd_bytes", "cache_slots", "page_size", "num_ssd",
-                         "cache_line"], list(v)))
+                         "cache_line", "shard_bytes"], list(v)))

@@ -92,6 +92,11 @@ def test_gather_refused_before_peers_attached():
     assert L.gids_read_feature(s, out.data_ptr(), d.data_ptr(), 4, 256, 256, 0, None) == gids_abi.GIDS_E_STATE
     h = ctypes.create_string_buffer(64)
     check(L.gids_store_ipc_handle(s, h, 64))
+    # the shard a peer maps through CUDA IPC is a whole number of 2 MB pages
+    # (an odd-sized one is mapped with small pages and read at a third of the link)
+    g = (ctypes.c_uint64 * 8)()
+    check(L.gids_store_geometry(s, g, 8))
+    assert g[7] > 0 and g[7] % (2 << 20) == 0
     check(L.gids_store_destroy(s))
     check(L.gids_ctrls_destroy(c))
 
