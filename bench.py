@@ -79,7 +79,8 @@ CONFIGS = {
 # hits; the full run has 45 %); a full launch's traffic is this times its rows. Other configs and
 # policies report null.
 TRAFFIC_PER_ROW = {("c2", "static"): 2.4666e9 / 366742}
-KIND = {"float32": 1, "float16": 2}
+# synthetic feature streams: fp32 uniform[-1, 1) (configs 1-3, 5), fp16 normal(0, 1) (config 4)
+KIND = {"float32": 1, "float16": 4}
 METRIC = "feature-gather GB/s (gathered rows x row bytes / gather time), all GPUs"
 DATA = "synthetic (seeded features, seeded synthetic graph + neighbour sampler; DGL and IGB absent)"
 TDTYPE = {"float32": torch.float32, "float16": torch.float16}

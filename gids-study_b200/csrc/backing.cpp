@@ -17,6 +17,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <thread>
@@ -288,7 +289,13 @@ void backing_read(const Controllers& c, void* dst, uint64_t nbytes, uint64_t off
 //   kind 1, fp32: top 24 bits k, value k * 2^-23 - 1 (uniform on [-1, 1));
 //   kind 2, fp16: m = (sum of the 8 bytes) - 1020, value m * 2^-8
 //                 (bell-shaped, mean 0, sd about 0.82, exact in fp16);
-//   kind 3, int64: the raw 64-bit output.
+//   kind 3, int64: the raw 64-bit output;
+//   kind 4, fp16: normal(0, 1) by the Box-Muller transform (Box and Muller,
+//                 Ann. Math. Statist. 1958) of the two 32-bit halves,
+//                 u1 = (hi + 1) 2^-32 in (0, 1], u2 = lo 2^-32 in [0, 1):
+//                 sqrt(-2 ln u1) cos(2 pi u2) in double, rounded to fp16 by
+//                 the compiler's _Float16 conversion (round to nearest even).
+//                 The host's libm computes it, here and in the oracle alike.
 namespace {
 constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ULL;
 inline uint64_t sm_mix(uint64_t z) {
@@ -313,9 +320,17 @@ inline uint16_t synth_f16(uint64_t h) {
   const int e = 31 - __builtin_clz(a);
   return (uint16_t)(sign | ((uint16_t)(e + 7) << 10) | (uint16_t)((a << (10 - e)) & 0x3FF));
 }
+inline uint16_t synth_f16_normal(uint64_t h) {
+  const double u1 = ((double)(h >> 32) + 1.0) * 0x1p-32;
+  const double u2 = (double)(h & 0xFFFFFFFFull) * 0x1p-32;
+  const _Float16 v = (_Float16)(std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+  uint16_t b;
+  memcpy(&b, &v, 2);
+  return b;
+}
 }  // namespace
 
-int synth_elem_bytes(int kind) { return kind == 1 ? 4 : kind == 2 ? 2 : kind == 3 ? 8 : 0; }
+int synth_elem_bytes(int kind) { return kind == 1 ? 4 : (kind == 2 || kind == 4) ? 2 : kind == 3 ? 8 : 0; }
 
 void backing_fill_synthetic(Controllers& c, int kind, uint64_t seed, int threads) {
   const int eb = synth_elem_bytes(kind);
@@ -334,6 +349,9 @@ void backing_fill_synthetic(Controllers& c, int kind, uint64_t seed, int threads
       } else if (kind == 2) {
         uint16_t* d = (uint16_t*)dst;
         for (uint64_t i = 0; i < per_page; i++) d[i] = synth_f16(synth_u64(seed, e0 + i));
+      } else if (kind == 4) {
+        uint16_t* d = (uint16_t*)dst;
+        for (uint64_t i = 0; i < per_page; i++) d[i] = synth_f16_normal(synth_u64(seed, e0 + i));
       } else {
         uint64_t* d = (uint64_t*)dst;
         for (uint64_t i = 0; i < per_page; i++) d[i] = synth_u64(seed, e0 + i);

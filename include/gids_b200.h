@@ -336,7 +336,8 @@ GIDS_API int gids_flush_cache(gids_store_t *s);
  * thread, gids_nvme.cu:764-770). */
 GIDS_API int gids_read_range_host(gids_store_t *s, void *dst, uint64_t nbytes, uint64_t offset_bytes);
 /* Fill the whole backing store with the synthetic feature stream `kind`
- * (1 = fp32 uniform[-1,1), 2 = fp16 byte-sum, 3 = int64 raw) of `seed`:
+ * (1 = fp32 uniform[-1,1), 2 = fp16 byte-sum, 3 = int64 raw, 4 = fp16
+ * normal(0,1) by Box-Muller) of `seed`:
  * element e of the range holds element (e mod wrap) of the stream, where
  * wrap covers the pages the SSDs physically hold. Uses `threads` host threads
  * (0 = all). No reference counterpart: the reference's SSDs are filled by

@@ -25,6 +25,7 @@
  * by running the reference's own memmap loader (IGB260M.paper_feat) and
  * torch.index_select; see tests/golden/make_golden.py.
  */
+#include <math.h>
 #include <pthread.h>
 #include <stdint.h>
 #include <string.h>
@@ -32,6 +33,7 @@
 #define GO_KIND_F32_UNIFORM 1
 #define GO_KIND_F16_BYTESUM 2
 #define GO_KIND_I64_RAW 3
+#define GO_KIND_F16_NORMAL 4
 
 #define GO_GOLDEN 0x9E3779B97F4A7C15ULL
 
@@ -49,6 +51,7 @@ int go_kind_elem_bytes(int kind) {
     case GO_KIND_F32_UNIFORM: return 4;
     case GO_KIND_F16_BYTESUM: return 2;
     case GO_KIND_I64_RAW: return 8;
+    case GO_KIND_F16_NORMAL: return 2;
     default: return 0;
   }
 }
@@ -78,6 +81,19 @@ static inline uint16_t go_f16_bits(uint64_t h) {
   return (uint16_t)(sign | (expf << 10) | mant);
 }
 
+/* normal(0, 1) by the Box-Muller transform (Box and Muller, 1958) of the
+ * hash's two 32-bit halves: u1 = (hi + 1) 2^-32 in (0, 1], u2 = lo 2^-32 in
+ * [0, 1), sqrt(-2 ln u1) cos(2 pi u2) in double, rounded to fp16 by the
+ * compiler's _Float16 conversion (round to nearest even) */
+static inline uint16_t go_f16_normal_bits(uint64_t h) {
+  double u1 = ((double)(h >> 32) + 1.0) * 0x1p-32;
+  double u2 = (double)(h & 0xFFFFFFFFull) * 0x1p-32;
+  _Float16 v = (_Float16)(sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2));
+  uint16_t b;
+  memcpy(&b, &v, 2);
+  return b;
+}
+
 /* writes the element e of `kind`/`seed` to dst (elem_bytes bytes) */
 static inline void go_synth_elem(int kind, uint64_t seed, uint64_t e, void *dst) {
   uint64_t h = go_synth_u64(seed, e);
@@ -86,6 +102,9 @@ static inline void go_synth_elem(int kind, uint64_t seed, uint64_t e, void *dst)
     memcpy(dst, &b, 4);
   } else if (kind == GO_KIND_F16_BYTESUM) {
     uint16_t b = go_f16_bits(h);
+    memcpy(dst, &b, 2);
+  } else if (kind == GO_KIND_F16_NORMAL) {
+    uint16_t b = go_f16_normal_bits(h);
     memcpy(dst, &b, 2);
   } else {
     memcpy(dst, &h, 8);

@@ -28,7 +28,9 @@ LIB_PATH = os.path.join(HERE, "_build", "libgids_oracle.so")
 KIND_F32_UNIFORM = 1
 KIND_F16_BYTESUM = 2
 KIND_I64_RAW = 3
-KIND_DTYPE = {KIND_F32_UNIFORM: np.float32, KIND_F16_BYTESUM: np.float16, KIND_I64_RAW: np.int64}
+KIND_F16_NORMAL = 4
+KIND_DTYPE = {KIND_F32_UNIFORM: np.float32, KIND_F16_BYTESUM: np.float16, KIND_I64_RAW: np.int64,
+              KIND_F16_NORMAL: np.float16}
 
 _lib = None
 

@@ -107,11 +107,12 @@ def test_capacity_wraps(built):
         check(L.gids_ctrls_destroy(c))
 
 
-@pytest.mark.parametrize("kind", [oracle.KIND_F32_UNIFORM, oracle.KIND_F16_BYTESUM, oracle.KIND_I64_RAW])
+@pytest.mark.parametrize("kind", [oracle.KIND_F32_UNIFORM, oracle.KIND_F16_BYTESUM, oracle.KIND_I64_RAW,
+                                  oracle.KIND_F16_NORMAL])
 def test_synthetic_fill_matches_oracle(built, kind):
     L = gids_abi.lib()
     page, n = 4096, 3
-    eb = {1: 4, 2: 2, 3: 8}[kind]
+    eb = {1: 4, 2: 2, 3: 8, 4: 2}[kind]
     rows, cdim = 300, 512
     nbytes = rows * cdim * eb
     c = controllers(n, capacity=(1 + 20) * page)  # wraps after 60 pages

@@ -92,7 +92,8 @@ def test_mmap_index_select_matches_oracle(tmp_path):
     assert same_bits(ref, oracle.gather(t, ids, dim=100, key_off=3))
 
 
-@pytest.mark.parametrize("kind", [oracle.KIND_F32_UNIFORM, oracle.KIND_F16_BYTESUM, oracle.KIND_I64_RAW])
+@pytest.mark.parametrize("kind", [oracle.KIND_F32_UNIFORM, oracle.KIND_F16_BYTESUM, oracle.KIND_I64_RAW,
+                                  oracle.KIND_F16_NORMAL])
 def test_gather_synth_equals_table_gather(kind):
     rows, cdim, dim = 300, 96, 64
     t = oracle.synth_table(kind, 4, rows, cdim)
@@ -157,3 +158,18 @@ def test_stripe_image_round_trip():
         c, dp = python_stripe(p, 4, 3, 0)
         back[p * page:(p + 1) * page] = devs[c][dp * page:(dp + 1) * page]
     assert np.array_equal(back, logical)
+
+
+def test_fp16_normal_stream():
+    """kind 4: normal(0, 1) by Box-Muller, rounded to fp16 (the config-4 features)."""
+    t = oracle.synth_table(oracle.KIND_F16_NORMAL, 5, 400, 768)
+    v = t.astype(np.float64)
+    assert np.isfinite(v).all()
+    assert abs(v.mean()) < 0.01 and abs(v.std() - 1.0) < 0.01
+    assert abs((np.abs(v) < 1.0).mean() - 0.6827) < 0.005 and abs((np.abs(v) < 2.0).mean() - 0.9545) < 0.003
+    # element 0 of seed 5 by hand: the same transform in float64, rounded by numpy's float16 (RNE)
+    h = int(oracle.synth_table(oracle.KIND_I64_RAW, 5, 1, 1).view(np.uint64)[0, 0])
+    u1 = ((h >> 32) + 1.0) * 2.0 ** -32
+    u2 = (h & 0xFFFFFFFF) * 2.0 ** -32
+    z = np.sqrt(-2.0 * np.log(u1)) * np.cos(6.283185307179586 * u2)
+    assert np.float16(z).view(np.uint16) == t[0, 0].view(np.uint16)
