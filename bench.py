@@ -134,6 +134,16 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
         return float(t.item())
 
+    def gather(self, v: float) -> list:
+        """v of every rank, in rank order"""
+        if self.pg is None:
+            return [v]
+        dev = torch.device("cuda", self.local) if self.pg.get_backend() == "nccl" else torch.device("cpu")
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [float(x.item()) for x in out]
+
     def close(self):
         if self.pg is not None:
             self.pg.destroy_process_group()
@@ -670,6 +680,12 @@ def run_ours(args, cfg, dist: Dist):
     last = None
     for i in range(args.warmup):
         last = g.fetch_feature(dim, dev_it, device)  # held like the timed loop's last step
+    # the caching allocator of a job that has been training holds blocks for its largest
+    # minibatch: two outputs of the largest timed minibatch (the timed loop holds the last
+    # step's features while the next step allocates), so no timed step waits on cudaMalloc
+    big = max(nrows(b) for b in batches[args.warmup:])
+    spare = [torch.empty((big, dim), dtype=TDTYPE[dt], device=device) for _ in range(2)]
+    del spare
     torch.cuda.synchronize()
     bam.reset_stats()
 
@@ -779,6 +795,7 @@ def run_ours(args, cfg, dist: Dist):
                           "second CUDA stream while the previous minibatch's gather runs"}
 
     # ---- aggregate over ranks
+    rank_ms = [round(x / max(1, len(dev_ids)) * 1e3, 3) for x in dist.gather(t_val)]
     t_val_max = dist.max(t_val)
     t_e2e_max = dist.max(t_e2e)
     rows_val_all = dist.sum(rows_val)
@@ -857,6 +874,7 @@ def run_ours(args, cfg, dist: Dist):
                      "cache_policy": args.policy,
                      "static_hot_rows": n_static or None,
                      "cache_warmup_minibatches": n_cw,
+                     "rank_ms_per_step": rank_ms,
                      "gather_grid_cap": args.gather_blocks or None},
         "parity": {"rows_checked": int(dist.sum(sum(p["rows_checked"] for p in parity))),
                    "ok": bool(dist.sum(0.0 if all(p["ok"] for p in parity) else 1.0) == 0.0),

@@ -1,5 +1,5 @@
 """Multi-rank host logic on CPU (gloo, world size 2): the bench's
-max/sum-over-ranks timing helpers, per-rank sampler seeds, and the CUDA IPC
+max/sum/gather-over-ranks timing helpers, per-rank sampler seeds, and the CUDA IPC
 handle exchange of a sharded GIDS (with a fake store recording what it got)."""
 import os
 import sys
@@ -23,6 +23,7 @@ def _worker(rank, world, port, q):
         d.init("gloo")
         t_max = d.max(1.0 + rank)
         s_sum = d.sum(10.0 * (rank + 1))
+        per_rank = d.gather(0.5 + rank)
         d.barrier()
 
         # sharded GIDS handle exchange with a fake store
@@ -62,7 +63,7 @@ def _worker(rank, world, port, q):
         g = gmod.GIDS(page_size=4096, cache_dim=64, num_ele=1000 * 64, shard_cache=True)
         names = [c[0] for c in g.BAM_FS.calls]
         opened = [c for c in g.BAM_FS.calls if c[0] == "open_peers"][0][1]
-        q.put((rank, t_max, s_sum, bench.sampler_seed(rank), g.world, g.rank, names, opened))
+        q.put((rank, t_max, s_sum, bench.sampler_seed(rank), g.world, g.rank, names, opened, per_rank))
         d.close()
     except Exception as e:
         q.put((rank, "error", repr(e)))
@@ -87,8 +88,9 @@ def test_two_ranks_gloo():
                 p.kill()
     for r in (0, 1):
         assert out[r][1] != "error", out[r]
-        _, t_max, s_sum, seed, world, grank, names, opened = out[r]
+        _, t_max, s_sum, seed, world, grank, names, opened, per_rank = out[r]
         assert t_max == 2.0 and s_sum == 30.0  # max and sum over both ranks
+        assert per_rank == [0.5, 1.5]  # every rank's value, in rank order
         assert seed == 1000 + r
         assert (world, grank) == (2, r)
         # sharding is set before init_controllers; handles arrive in rank order
