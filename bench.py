@@ -580,7 +580,7 @@ def run_ours(args, cfg, dist: Dist):
                   wb_size=max(1, cfg["wb"]), cache_line=cfg["line"] or None,
                   heterograph=cfg["hetero"] is not None, heterograph_map=hmap,
                   cache_admission=POLICIES[args.policy][0], cache_ref_max=POLICIES[args.policy][1],
-                  gather_blocks=args.gather_blocks)
+                  gather_blocks=args.gather_blocks, wb_prefetch=args.wb_prefetch and cfg["wb"] > 0)
     t_store = time.time() - t0
     if not shared:
         t0 = time.time()
@@ -806,7 +806,9 @@ def run_ours(args, cfg, dist: Dist):
     n_launch = max(1, launches)
     t_launch = k_ms / 1e3 / n_launch
     rows_l = st["rows"] / n_launch
-    r_host = (st["bytes_miss"] + st["bytes_bypass"] + st["bytes_cpu"]) / n_launch
+    # host bytes: rows read through or filled by the gathers, constant-CPU-buffer rows, and the
+    # lines window-buffer prefetch launches read into the cache
+    r_host = (st["bytes_miss"] + st["bytes_bypass"] + st["bytes_cpu"] + st.get("prefetched", 0) * line) / n_launch
     r_hbm_src = st["bytes_hit"] / n_launch
     alg_hbm = r_hbm_src + rows_l * row_bytes + 8 * rows_l  # source reads of hits + output writes + ids
     r_peer = st.get("bytes_peer", 0) / n_launch  # hit bytes read from other ranks' shards over NVLink
@@ -875,7 +877,8 @@ def run_ours(args, cfg, dist: Dist):
                      "static_hot_rows": n_static or None,
                      "cache_warmup_minibatches": n_cw,
                      "rank_ms_per_step": rank_ms,
-                     "gather_grid_cap": args.gather_blocks or None},
+                     "gather_grid_cap": args.gather_blocks or None,
+                     "window_buffer_prefetch": bool(args.wb_prefetch and cfg["wb"] > 0)},
         "parity": {"rows_checked": int(dist.sum(sum(p["rows_checked"] for p in parity))),
                    "ok": bool(dist.sum(0.0 if all(p["ok"] for p in parity) else 1.0) == 0.0),
                    "against": "oracle.gather_synth: the reference's gather restated over the same synthetic "
@@ -994,6 +997,8 @@ def main():
     ap.add_argument("--shared-backing", action="store_true",
                     help="back the emulated SSDs with shared /dev/shm files even on one GPU (as N>1 runs do)")
     ap.add_argument("--gather-blocks", type=int, default=0, help="cap on the gather kernel's grid (0: all resident)")
+    ap.add_argument("--wb-prefetch", action="store_true",
+                    help="window-buffered configs: fetch each batch's lines into the cache as it enters the window")
     ap.add_argument("--cache-warmup", type=int, default=-1,
                     help="untimed minibatches (other sampler seeds) gathered before the warm-up steps; -1: "
                          "enough for about 12 cache-sizes of line references, at most 60")

@@ -100,13 +100,19 @@ class GIDS:
     second-chance clock). Neither changes what is gathered. ``gather_blocks``
     caps the gather kernel's grid (0: every block the GPU holds at once), so a
     gather bound by the host link leaves SMs to kernels on other streams.
+    ``wb_prefetch`` (with ``window_buffer``; default False) also fetches into
+    the cache, as each batch enters the window, the lines of it that its
+    gather would insert (a prefetch launch on the current stream that copies
+    nothing out), so that the gather, ``wb_size`` batches later, finds them
+    resident; the reference's window buffering only protects marked pages
+    from eviction.
     """
 
     def __init__(self, page_size=4096, off=0, cache_dim=1024, num_ele=300 * 1000 * 1000 * 1024, num_ssd=1,
                  ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
                  long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
                  ssd_path=None, synchronous=False, shard_cache=False, process_group=None, cache_line=None,
-                 cache_admission=True, cache_ref_max=3, gather_blocks=0):
+                 cache_admission=True, cache_ref_max=3, gather_blocks=0, wb_prefetch=False):
         if dtype is None:
             dtype = torch.int64 if long_type else torch.float32
         if dtype not in _STORE_CLASSES:
@@ -125,6 +131,8 @@ class GIDS:
         self.window_buffer = []
         self.wb_init = False
         self.wb_size = wb_size
+        self.wb_prefetch = wb_prefetch
+        self._wb_dim = cache_dim  # columns the gathers read: the prefetch fetches those rows' lines
 
         self.page_size = page_size
         # byte offset -> first page on every SSD (GIDS.py:583)
@@ -237,10 +245,17 @@ class GIDS:
                     else:
                         print("Cannot find key: ", key, " in the heterograph map!")
                 self.BAM_FS.set_window_buffering(input_tensor.data_ptr(), len(input_tensor), int(key_off), stream)
+                self._prefetch(input_tensor, int(key_off), stream)
         else:
             input_tensor = _as_index(batch[0], self.device)
             self.BAM_FS.set_window_buffering(input_tensor.data_ptr(), len(input_tensor), 0, stream)
+            self._prefetch(input_tensor, 0, stream)
         self.WB_time += time.time() - s_time
+
+    def _prefetch(self, ids, key_off, stream):
+        """Window-buffer prefetch (extension): bring the lines of rows ``ids`` into the cache."""
+        if self.wb_prefetch and len(ids):
+            self.BAM_FS.prefetch(ids.data_ptr(), len(ids), self._wb_dim, self.cache_dim, key_off, stream)
 
     def fill_wb(self, it, num):
         """Pull ``num`` batches ahead and mark them (GIDS.py:752-769)."""
@@ -324,6 +339,7 @@ class GIDS:
         """Next batch from ``it`` with its gathered features appended (GIDS.py:791-1058)."""
         GIDS_time_start = time.time()
         stream = _current_stream_handle(self.device)
+        self._wb_dim = dim
 
         if self.window_buffering_flag and not self.wb_init:
             self.fill_wb(it, self.wb_size)

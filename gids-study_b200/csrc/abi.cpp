@@ -306,6 +306,19 @@ int gids_read_feature(gids_store_t* s, void* out, const int64_t* idx, int64_t n,
   });
 }
 
+int gids_prefetch(gids_store_t* s, const int64_t* idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
+                  void* stream) {
+  return guarded([&] {
+    NEED(s);
+    GIDS_CHECK(n >= 0, GIDS_E_INVAL, "n must be >= 0");
+    void* outs[1] = {nullptr};
+    const int64_t* idxs[1] = {idx};
+    uint64_t ns[1] = {(uint64_t)n};
+    uint64_t ko[1] = {key_off};
+    s->s.read_multi(1, outs, idxs, ns, dim, cache_dim, ko, (cudaStream_t)stream, true);
+  });
+}
+
 int gids_read_feature_multi(gids_store_t* s, int k, void* const* outs, const int64_t* const* idxs,
                             const uint64_t* ns, int dim, int cache_dim, const uint64_t* key_offs, void* stream) {
   return guarded([&] {

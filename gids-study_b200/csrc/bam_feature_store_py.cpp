@@ -132,6 +132,10 @@ class FeatureStore {
   void unset_window_buffering(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
     check(gids_unset_window_buffering(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
   }
+  // extension: window-buffer prefetch, the rows' lines brought into the cache without an output
+  void prefetch(uint64_t idx, int64_t n, int dim, int cache_dim, int64_t key_off, uint64_t stream) {
+    check(gids_prefetch(s(), (const int64_t*)idx, n, dim, cache_dim, (uint64_t)key_off, (void*)stream));
+  }
   // extension: permanent pins of the rows' cache lines (a static hot set)
   void pin_rows(uint64_t idx, int64_t n, int64_t hash_off, uint64_t stream) {
     check(gids_store_pin_rows(s(), (const int64_t*)idx, n, hash_off, 0, (void*)stream));
@@ -240,7 +244,9 @@ class FeatureStore {
     static const char* names[] = {"access",      "hit",       "miss",          "read_io",     "bypass",
                                   "cpu_rows",    "rows",      "wait_timeouts", "bad_ids",     "bytes_hit",
                                   "bytes_miss",  "bytes_bypass", "bytes_cpu",   "evictions",   "launches",
-                                  "bytes_peer",  "ns_lookup", "ns_fill_wait",  "ns_copy",     "ns_release"};
+                                  "bytes_peer",  "ns_lookup", "ns_fill_wait",  "ns_copy",     "ns_release",
+                                  "prefetched"};
+    static_assert(sizeof(names) / sizeof(names[0]) == GIDS_STAT_COUNT, "one name per counter");
     for (int i = 0; i < GIDS_STAT_COUNT; i++) d[names[i]] = v[i];
     return d;
   }
@@ -317,6 +323,8 @@ void bind_store(py::module_& m, const char* name) {
            py::arg("hash_off") = 0, py::arg("stream") = 0, R())
       .def("unset_window_buffering", &S::unset_window_buffering, py::arg("id_idx"), py::arg("num_pages"),
            py::arg("hash_off") = 0, py::arg("stream") = 0, R())
+      .def("prefetch", &S::prefetch, py::arg("i_index_ptr"), py::arg("num_index"), py::arg("dim"),
+           py::arg("cache_dim") = 1024, py::arg("key_off") = 0, py::arg("stream") = 0, R())
       .def("pin_rows", &S::pin_rows, py::arg("id_idx"), py::arg("num"), py::arg("hash_off") = 0,
            py::arg("stream") = 0, R())
       .def("unpin_rows", &S::unpin_rows, py::arg("id_idx"), py::arg("num"), py::arg("hash_off") = 0,

@@ -444,7 +444,7 @@ __device__ __forceinline__ void wb_consume(unsigned int* w, unsigned int cnt) {
 
 enum {
   K_ROWS, K_CPU, K_BAD, K_ACCESS, K_HIT, K_MISS, K_BYPASS, K_READIO, K_TIMEOUT,
-  K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_BPEER,
+  K_BHIT, K_BMISS, K_BBYP, K_BCPU, K_EVICT, K_BPEER, K_PREFETCH,
 #ifdef GIDS_PHASE_TIMERS
   K_TLOOK, K_TFILL, K_TCOPY, K_TREL,
 #endif
@@ -455,6 +455,7 @@ __constant__ int kStatMap[K_N] = {GIDS_STAT_ROWS,       GIDS_STAT_CPU_ROWS,     
                                   GIDS_STAT_BYPASS,     GIDS_STAT_READ_IO,      GIDS_STAT_WAIT_TIMEOUT,
                                   GIDS_STAT_BYTES_HIT,  GIDS_STAT_BYTES_MISS,   GIDS_STAT_BYTES_BYPASS,
                                   GIDS_STAT_BYTES_CPU,  GIDS_STAT_EVICTIONS,    GIDS_STAT_BYTES_PEER,
+                                  GIDS_STAT_PREFETCHED,
 #ifdef GIDS_PHASE_TIMERS
                                   GIDS_STAT_NS_LOOKUP,  GIDS_STAT_NS_FILL,      GIDS_STAT_NS_COPY,
                                   GIDS_STAT_NS_RELEASE,
@@ -476,7 +477,10 @@ __device__ __forceinline__ unsigned long long phase_clock() {
 #define GIDS_PHASE_MARK(v)
 #endif
 
-template <int VEC, bool SYS>
+// PF: a prefetch launch (window-buffer prefetch): the tuples have no output;
+// the rows' lines are brought into the cache and nothing is copied out. It is
+// a separate instantiation so that the gather itself carries none of it.
+template <int VEC, bool SYS, bool PF = false>
 __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_constant__ GatherArgs a) {
   __shared__ SegDesc seg_sh[WARPS][32];
   __shared__ unsigned long long cnt_sh[WARPS][K_N];  // warp-private counters
@@ -518,6 +522,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
   for (uint64_t chunk = (uint64_t)blockIdx.x * WARPS + wib; chunk < a.total_chunks; chunk += n_warps) {
     while (ti + 1 < a.k && a.t[ti + 1].chunk_begin <= chunk) ti++;
     const GatherTuple& T = a.t[ti];
+    constexpr bool pf = PF;
     const uint64_t row = (chunk - T.chunk_begin) * rpc + ((uint32_t)lane >> seg_shift);
     const uint32_t sidx = (uint32_t)lane & seg_mask;
     const bool row_ok = row < T.n;
@@ -591,11 +596,17 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
           // pinned-only policy the cache holds the permanently pinned lines
           // alone and every other line is read through.
           bool admit = true;
+          // A prefetch applies the same rule without setting the admission
+          // bit: it inserts the lines the gather would insert (pinned for a
+          // later batch, or missed before in this window) ahead of time, and
+          // leaves lines the gather would read through to that gather, so the
+          // cache holds what it would hold without the prefetch.
           if (a.c.pinned_only) {
             admit = S.wb && (ld_relaxed_u32<SYS>(S.wb + lp) & WB_PERMANENT) != 0u;
           } else if (gate_sh[owner] && !(S.wb && ld_relaxed_u32<SYS>(S.wb + lp) > cnt)) {
             const unsigned long long bit = 1ull << (lp & 63);
-            admit = (atom_or_relaxed<SYS>(S.seen + (lp >> 6), bit) & bit) != 0;
+            admit = ((pf ? ld_relaxed<SYS>(S.seen + (lp >> 6)) : atom_or_relaxed<SYS>(S.seen + (lp >> 6), bit)) &
+                     bit) != 0;
           }
           if (!admit) {
             cls = CLS_BYPASS;
@@ -615,7 +626,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     }
 
     // output row and, for cache-path lanes, the segment's place in its page
-    char* const orow = row_ok ? T.out + row * (uint64_t)a.row_bytes : nullptr;
+    char* const orow = row_ok && !pf ? T.out + row * (uint64_t)a.row_bytes : nullptr;
     const uint32_t in_pg = seg_ok ? (uint32_t)((b0 + s0) - (p << shift)) : 0u;
     bool forwarded = false;
 
@@ -738,11 +749,11 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
                 const uint32_t ow = __shfl_sync(0xffffffffu, owner, o);
                 dq = a.c.sh[ow].slots + (so << shift);
                 mm = __shfl_sync(0xffffffffu, eq, o);  // lanes whose rows read line j
-                if (VEC == 16 && ((mm >> lane) & 1u)) forwarded = true;
+                if (VEC == 16 && !pf && ((mm >> lane) & 1u)) forwarded = true;
               }
               const uint32_t off = (((uint32_t)q << 9) + ((uint32_t)lane << 4)) & (a.c.page_size - 1u);
               __stcg(reinterpret_cast<int4*>(dq + off), v[q]);
-              if (VEC == 16) {  // fill-forward: the rows of line j straight from registers
+              if (VEC == 16 && !pf) {  // fill-forward: the rows of line j straight from registers
                 unsigned rest = mm;
                 while (rest) {
                   const int m = __ffs(rest) - 1;
@@ -763,6 +774,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
             // to this lane by __syncwarp) before the VALID bit
             red_add_release<SYS>(stw, ((unsigned long long)slot << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
             atomicAdd(acc + K_READIO, 1ull);
+            if (pf) atomicAdd(acc + K_PREFETCH, 1ull);
           }
           __syncwarp();
         }
@@ -774,7 +786,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         const unsigned long long so = __shfl_sync(0xffffffffu, (unsigned long long)slot, o);
         const uint32_t ow = __shfl_sync(0xffffffffu, owner, o);
         const unsigned mem = __shfl_sync(0xffffffffu, eq, o);  // lanes whose rows read line po
-        if (VEC == 16) {
+        if (VEC == 16 && !pf) {
           fill_page<true>(backing_addr(a.b, po, shift), a.c.sh[ow].slots + (so << shift), a.c.page_size, lane, mem,
                           in_pg, s1 - s0, orow + s0);
           if ((mem >> lane) & 1u) forwarded = true;
@@ -786,11 +798,14 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         if (lane == o) {
           red_add_release<SYS>(stw, (so << ST_SLOT_SHIFT) + (ST_VALID - ST_BUSY));
           acc[K_READIO]++;  // only lane o touches it here
+          if (pf) acc[K_PREFETCH]++;
         }
       }
     }
 
-    // ---- 4. bounded wait for pages filled by other warps (or other GPUs)
+    // ---- 4. bounded wait for pages filled by other warps (or other GPUs);
+    //         a prefetch does not wait: the line is on its way into the cache
+    if (pf && cls == CLS_WAIT) cls = CLS_BYPASS;
     if (__any_sync(0xffffffffu, cls == CLS_WAIT)) {
       unsigned ns = 32;
       for (uint32_t it = 0;; it++) {
@@ -820,7 +835,9 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const char* src = nullptr;
     char* dst = nullptr;
     uint32_t len = 0;
-    if (bad && sidx == 0) {
+    if (pf) {
+      // a prefetch copies nothing out
+    } else if (bad && sidx == 0) {
       len = a.row_bytes;  // zero row
       dst = orow;
     } else if (pinned && sidx == 0) {
@@ -889,7 +906,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
         const unsigned char rr = S.slot_ref[gslot];
         if (rr < a.c.ref_max) S.slot_ref[gslot] = rr + 1;
       }
-      if (S.wb) wb_consume<SYS>(S.wb + lp, cnt);
+      if (S.wb && !pf) wb_consume<SYS>(S.wb + lp, cnt);  // the gather of the row consumes its pins
     }
 
 #ifdef GIDS_PHASE_TIMERS
@@ -905,7 +922,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     }
 #endif
     // ---- counters
-    if (bad && sidx == 0) *reinterpret_cast<volatile int*>(a.host_err) = 1;
+    if (bad && sidx == 0 && !pf) *reinterpret_cast<volatile int*>(a.host_err) = 1;
     const unsigned r0 = sidx == 0;
     const bool cached = seg_ok && (gcls == CLS_HIT || gcls == CLS_OWN || gcls == CLS_WAITED);
     const unsigned n_rows_c = __popc(__ballot_sync(0xffffffffu, row_ok && r0));
@@ -922,7 +939,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     const unsigned lc = __reduce_add_sync(0xffffffffu, pinned && r0 ? len : 0u);
     const unsigned lpeer = SYS ? __reduce_add_sync(0xffffffffu, cached && owner != a.c.rank && !forwarded ? sl : 0u)
                                : 0u;
-    if (lane == 0) {
+    if (lane == 0 && !pf) {  // a prefetch counts only the lines it inserted
       acc[K_ROWS] += n_rows_c;
       acc[K_CPU] += n_cpu;
       acc[K_BAD] += n_bad;
@@ -1057,7 +1074,11 @@ static void allow_tma_ring() {
 }
 
 template <bool SYS>
-static void launch_scoped(const GatherArgs& a, int vec, int grid, cudaStream_t st) {
+static void launch_scoped(const GatherArgs& a, int vec, int grid, cudaStream_t st, bool prefetch) {
+  if (prefetch) {  // copies nothing out: no TMA ring, any vector width
+    gather_kernel<8, SYS, true><<<grid, GATHER_THREADS, 0, st>>>(a);
+    return;
+  }
   switch (vec) {
     case 16:
       allow_tma_ring<SYS>();
@@ -1070,11 +1091,11 @@ static void launch_scoped(const GatherArgs& a, int vec, int grid, cudaStream_t s
   }
 }
 
-void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st) {
+void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st, bool prefetch) {
   if (sys)
-    launch_scoped<true>(a, vec, grid, st);
+    launch_scoped<true>(a, vec, grid, st, prefetch);
   else
-    launch_scoped<false>(a, vec, grid, st);
+    launch_scoped<false>(a, vec, grid, st, prefetch);
   GIDS_CUDA(cudaGetLastError());
 }
 

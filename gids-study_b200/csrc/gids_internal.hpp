@@ -166,7 +166,7 @@ struct WbArgs {
 
 // Launchers (gather.cu). sys = the cache is shared with other GPUs, so
 // state-word atomics and fences use system scope.
-void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st);
+void launch_gather(const GatherArgs& a, int vec, bool sys, int grid, cudaStream_t st, bool prefetch = false);
 void launch_wb_mark(const WbArgs& a, cudaStream_t st);
 void launch_host_probe(const DevBacking& b, uint64_t n_lines, uint32_t line_shift, uint32_t read_bytes,
                        uint64_t reads, void* dst, uint64_t dst_bytes, uint64_t seed, cudaStream_t st);
@@ -246,8 +246,10 @@ class Store {
   ~Store();
   void init_controllers(Controllers* c, uint32_t page_size, uint64_t read_off_pages, uint64_t cache_mb,
                         uint64_t num_ele, uint64_t num_ssd);
+  // prefetch: outs are ignored (null tuples): the rows' lines are brought into
+  // the cache and nothing is copied out (window-buffer prefetch)
   void read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
-                  int cache_dim, const uint64_t* key_offs, cudaStream_t st);
+                  int cache_dim, const uint64_t* key_offs, cudaStream_t st, bool prefetch = false);
   // mode WB_MARK: mark the rows' lines (one pin per row and line); WB_UNMARK:
   // take those marks back (a window that will not be gathered); WB_PIN /
   // WB_UNPIN: set / clear the lines' permanent pins

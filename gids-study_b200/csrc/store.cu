@@ -357,9 +357,9 @@ void Store::set_row_layout(uint32_t cache_dim) {
 }
 
 void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, const uint64_t* ns, int dim,
-                       int cache_dim, const uint64_t* key_offs, cudaStream_t st) {
+                       int cache_dim, const uint64_t* key_offs, cudaStream_t st, bool prefetch) {
   std::lock_guard<std::mutex> lk(mu);
-  NvtxRange nv("gids.read_feature");
+  NvtxRange nv(prefetch ? "gids.prefetch" : "gids.read_feature");
   GIDS_CHECK(initialized, GIDS_E_STATE, "read_feature before init_controllers");
   GIDS_CHECK(shards_ready, GIDS_E_STATE, "sharded cache: peer shards not attached yet");
   GIDS_CHECK(k >= 0, GIDS_E_INVAL, "k must be >= 0");
@@ -389,13 +389,13 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
   int vec = 16;
   auto fits = [&](uint64_t v) { return v % vec == 0; };
   while (vec > 2 && !(fits(row_bytes) && fits(src_stride))) vec >>= 1;
-  for (int i = 0; i < k; i++)
+  for (int i = 0; i < k && !prefetch; i++)
     while (vec > 2 && (uint64_t)(uintptr_t)outs[i] % vec) vec >>= 1;
   GIDS_CHECK(row_bytes % vec == 0 && src_stride % vec == 0, GIDS_E_INVAL, "rows must be 2-byte aligned");
   for (int i = 0; i < k; i++) {
-    GIDS_CHECK(ns[i] == 0 || (outs[i] && idxs[i]), GIDS_E_INVAL, "null output or index pointer");
+    GIDS_CHECK(ns[i] == 0 || ((prefetch || outs[i]) && idxs[i]), GIDS_E_INVAL, "null output or index pointer");
     GIDS_CHECK((uintptr_t)idxs[i] % 8 == 0 || ns[i] == 0, GIDS_E_INVAL, "index array must be 8-byte aligned");
-    GIDS_CHECK((uintptr_t)outs[i] % vec == 0 || ns[i] == 0, GIDS_E_INVAL, "output not aligned");
+    GIDS_CHECK(prefetch || (uintptr_t)outs[i] % vec == 0 || ns[i] == 0, GIDS_E_INVAL, "output not aligned");
   }
 
   GatherArgs a;
@@ -412,7 +412,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
   a.spin_limit = wait_limit;
   a.sweep_limit = 64;
   uint64_t rows_total = 0;
-  if (admission == 1 && n_slots) {
+  if (admission == 1 && n_slots && !prefetch) {
     // age the admission bits: clear this shard's after 2 x n_slots line references
     uint64_t refs = 0;
     for (int i = 0; i < k; i++) refs += ns[i] * max_pages;
@@ -432,7 +432,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
       if (!n) continue;
       GatherTuple& t = a.t[used++];
       t.idx = idxs[base + i];
-      t.out = (char*)outs[base + i];
+      t.out = prefetch ? nullptr : (char*)outs[base + i];  // no output: the kernel only fills
       t.n = n;
       t.key_off = key_offs ? key_offs[base + i] : 0;
       t.chunk_begin = chunks;
@@ -445,7 +445,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
     }
     a.k = used;
     a.total_chunks = chunks;
-    const int vi = vec == 16 ? 0 : vec == 8 ? 1 : vec == 4 ? 2 : 3;
+    const int vi = prefetch ? 1 : vec == 16 ? 0 : vec == 8 ? 1 : vec == 4 ? 2 : 3;  // prefetch: the 8-byte kernel's grid
     const uint64_t want_blocks = (chunks + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
     uint64_t cap = (uint64_t)grid_blocks[world > 1 ? 1 : 0][vi];
     if (max_blocks) cap = std::min<uint64_t>(cap, max_blocks);
@@ -459,13 +459,13 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
       GIDS_CUDA(cudaEventCreate(&ev.b));
     }
     GIDS_CUDA(cudaEventRecord(ev.a, st));
-    launch_gather(a, vec, world > 1, grid, st);
+    launch_gather(a, vec, world > 1, grid, st, prefetch);
     launches++;
     GIDS_CUDA(cudaEventRecord(ev.b, st));
     ev_pending.push_back(ev);
     if (k == 0) break;
   }
-  total_access += rows_total;
+  if (!prefetch) total_access += rows_total;
   last_stream = st;
   if (synchronous) {
     GIDS_CUDA(cudaStreamSynchronize(st));

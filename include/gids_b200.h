@@ -244,6 +244,24 @@ GIDS_API int gids_set_window_buffering(gids_store_t *s, const int64_t *idx, int6
  * every pin of the calling rank's shard. */
 GIDS_API int gids_unset_window_buffering(gids_store_t *s, const int64_t *idx, int64_t n, int64_t hash_off,
                                          uint32_t row_stride_elems, void *stream);
+/* Window-buffer prefetch (no reference counterpart: the reference's window
+ * buffering only protects marked pages from eviction,
+ * page_cache_backup.h:1265-1272). The gather of gids_read_feature for rows
+ * (idx[i] + key_off), dim / cache_dim as there, without an output: the rows'
+ * cache lines are looked up, and every missing line that the gather would
+ * insert is read from the backing store into a slot now, so a later gather of
+ * the rows finds it resident. The rule is the gather's: every line while the
+ * cache fills; once it is full, lines pinned for a later batch (more window
+ * pins than this call's references) or missed before in the admission window;
+ * with admission = 2, permanently pinned lines. The prefetch sets no admission
+ * bit, and lines the gather would read through are left to it, so the cache
+ * ends up holding what it would hold without the prefetch. Nothing is copied out, no
+ * window-buffer pin is consumed (call it after gids_set_window_buffering for
+ * the same rows, so the lines stay until their gather), bad ids and rows of
+ * the constant CPU buffer are skipped. Stream-ordered on `stream`; lines it
+ * inserts count in GIDS_STAT_PREFETCHED and GIDS_STAT_READ_IO, nothing else. */
+GIDS_API int gids_prefetch(gids_store_t *s, const int64_t *idx, int64_t n, int dim, int cache_dim, uint64_t key_off,
+                           void *stream);
 /* Permanent pins (no reference counterpart; the reference keeps its hot set
  * in the constant CPU buffer instead, gids_cpu_backing_buffer): the cache
  * lines of rows (idx[i] + hash_off) (device int64 array; rows map to lines by
@@ -301,7 +319,8 @@ GIDS_API int gids_flush_cpu_access_count(gids_store_t *s);
 #define GIDS_STAT_NS_FILL 17
 #define GIDS_STAT_NS_COPY 18
 #define GIDS_STAT_NS_RELEASE 19
-#define GIDS_STAT_COUNT 20
+#define GIDS_STAT_PREFETCHED 20  /* lines inserted by gids_prefetch (also counted in READ_IO) */
+#define GIDS_STAT_COUNT 21
 /* Copies the cumulative counters (synchronizes the store's last stream). */
 GIDS_API int gids_get_stats(gids_store_t *s, uint64_t *out, int count);
 GIDS_API int gids_reset_stats(gids_store_t *s);

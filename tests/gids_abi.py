@@ -16,8 +16,9 @@ GIDS_E_RANGE = -5
 GIDS_E_IO = -6
 GIDS_E_UNSUPPORTED = -7
 STAT_NAMES = ["access", "hit", "miss", "read_io", "bypass", "cpu_rows", "rows", "wait_timeouts", "bad_ids",
-              "bytes_hit", "bytes_miss", "bytes_bypass", "bytes_cpu", "evictions", "launches", "bytes_peer"]
-N_STATS = 20
+              "bytes_hit", "bytes_miss", "bytes_bypass", "bytes_cpu", "evictions", "launches", "bytes_peer",
+              "ns_lookup", "ns_fill_wait", "ns_copy", "ns_release", "prefetched"]
+N_STATS = 21
 
 _lib = None
 
@@ -50,6 +51,7 @@ def lib():
             "gids_read_feature": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
             "gids_read_feature_multi": (i32, [vp, i32, P(vp), P(vp), P(u64), i32, i32, P(u64), vp]),
             "gids_read_feature_noalloc": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
+            "gids_prefetch": (i32, [vp, vp, i64, i32, i32, u64, vp]),
             "gids_set_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_unset_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_store_pin_rows": (i32, [vp, vp, i64, i64, u32, vp]),

@@ -79,6 +79,13 @@ def test_pybind_module_surface(built):
     s = B.BAM_Feature_Store_float()
     with pytest.raises(RuntimeError):
         s.read_feature(0, 0, 0, 1, 1, 0)  # before init_controllers
+    # every method that releases the GIL raises its error as a Python exception
+    # (a method that released it twice would abort the interpreter instead)
+    for call in (lambda: s.prefetch(0, 0, 1, 1, 0, 0), lambda: s.set_window_buffering(0, 0, 0, 0),
+                 lambda: s.unset_window_buffering(0, 0, 0, 0), lambda: s.pin_rows(0, 0, 0, 0),
+                 lambda: s.read_feature_hetero(0, [], [], [], 1, 1, [], 0)):
+        with pytest.raises(RuntimeError):
+            call()
 
 
 def test_gids_surface(built):

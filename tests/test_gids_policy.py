@@ -77,6 +77,9 @@ class FakeStore:
     def set_window_buffering(self, ptr, n, off, stream=0):
         self.calls.append(("wb", tuple(self._ids(ptr, n)), off))
 
+    def prefetch(self, ptr, n, dim, cache_dim, key_off, stream=0):
+        self.calls.append(("prefetch", tuple(self._ids(ptr, n)), dim, cache_dim, key_off))
+
     def set_cpu_buffer(self, ptr, num):
         self.cpu_pins = self._ids(ptr, num)
         self.calls.append(("set_cpu_buffer", num))
@@ -182,6 +185,26 @@ def test_window_buffering_marks_ahead(fake):
     assert len(wb) == 7 and wb[-1][1] == tuple(bs[6][0].numpy())
 
 
+def test_window_buffer_prefetch_follows_each_mark(fake):
+    g = fake(window_buffer=True, wb_size=2, wb_prefetch=True)
+    bs = batches(5, 20)
+    it = iter([list(b) for b in bs])
+    for i in range(2):
+        out = g.fetch_feature(48, it, "cpu")
+        assert np.array_equal(out[-1].numpy(), oracle.gather(FakeStore.table, bs[i][0].numpy(), dim=48))
+    ev = [c for c in g.BAM_FS.calls if c[0] in ("wb", "prefetch", "read_feature")]
+    # every batch entering the window is marked, then prefetched with the gathers' columns
+    marks = [c for c in ev if c[0] == "wb"]
+    pref = [c for c in ev if c[0] == "prefetch"]
+    assert [c[1] for c in pref] == [c[1] for c in marks] == [tuple(b[0].numpy()) for b in bs[:4]]
+    assert all(c[2:] == (48, 64, 0) for c in pref)
+    assert [c[0] for c in ev[:4]] == ["wb", "prefetch", "wb", "prefetch"]
+    # without the flag nothing is prefetched
+    g2 = fake(window_buffer=True, wb_size=2)
+    g2.fetch_feature(64, iter([list(b) for b in bs]), "cpu")
+    assert not [c for c in g2.BAM_FS.calls if c[0] == "prefetch"]
+
+
 def test_accumulator_merges_until_threshold(fake):
     g = fake(accumulator_flag=True)
     g.set_required_storage_access(bw=1.0, l_ssd=10, l_system=5, num_ssd=1, p=0.5)
@@ -235,6 +258,10 @@ def test_heterograph_window_buffering_skips_empty(fake):
     g.fetch_feature(64, iter([b1, b2]), "cpu")
     wb = [c for c in g.BAM_FS.calls if c[0] == "wb"]
     assert wb == [("wb", (1, 2), 0), ("wb", (3,), 0), ("wb", (4,), 500)]
+    g = fake(heterograph=True, heterograph_map=hmap, window_buffer=True, wb_size=1, wb_prefetch=True)
+    g.fetch_feature(64, iter([b1, b2]), "cpu")
+    pf = [c for c in g.BAM_FS.calls if c[0] == "prefetch"]
+    assert pf == [("prefetch", (1, 2), 64, 64, 0), ("prefetch", (3,), 64, 64, 0), ("prefetch", (4,), 64, 64, 500)]
 
 
 def test_out_of_scope_methods_raise(fake):
