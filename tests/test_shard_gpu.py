@@ -124,6 +124,31 @@ def test_in_process_shards_one_gpu(world):
         sh.close()
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_in_process_shards_prefetch(world):
+    """A prefetch by one rank fills the owners' shards; every rank's gather then hits."""
+    rows, cdim = 6000, 1024
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 27, rows, cdim)
+    sh = Shared(t, world, cache_mb=64, admission=False)
+    L = gids_abi.lib()
+    try:
+        ids = np.random.default_rng(world + 10).integers(0, rows, size=3000)
+        d = torch.as_tensor(ids, dtype=torch.int64).cuda()
+        check(L.gids_reset_stats(sh.s[0]))
+        check(L.gids_prefetch(sh.s[0], ctypes.c_void_p(d.data_ptr()), len(ids), cdim, cdim, 0, None))
+        torch.cuda.synchronize()
+        st = sh.stats(0)
+        assert st["rows"] == 0 and st["read_io"] == len(np.unique(ids))  # every distinct line, in its owner's shard
+        for r in range(world):
+            check(L.gids_reset_stats(sh.s[r]))
+            out = sh.gather(r, ids, cdim, cdim)
+            assert bits_equal(out, oracle.gather(t, ids))
+            st = sh.stats(r)
+            assert st["miss"] == 0 and st["bypass"] == 0 and st["hit"] == st["access"]
+    finally:
+        sh.close()
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_in_process_shards_churn(world):
     rows, cdim = 12000, 1024
