@@ -902,11 +902,15 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
     // ---- release, clock reference bit, window-buffer consumption
     if (took_ref && !keep_refs) {
       red_add_release<SYS>(stw, (unsigned long long)(-(long long)cnt));
-      if (gcls != CLS_BYPASS) {  // one more chance, up to the ceiling
+      // one more chance, up to the ceiling (the static policy holds only
+      // permanently pinned lines, which the clock never evicts: no counter)
+      if (gcls != CLS_BYPASS && !a.c.pinned_only) {
         const unsigned char rr = S.slot_ref[gslot];
         if (rr < a.c.ref_max) S.slot_ref[gslot] = rr + 1;
       }
-      if (S.wb && !pf) wb_consume<SYS>(S.wb + lp, cnt);  // the gather of the row consumes its pins
+      // the gather of the row consumes its window pins (none to read unless
+      // window buffering has marked lines since the pins were last cleared)
+      if (S.wb && !pf && a.c.wb_marks) wb_consume<SYS>(S.wb + lp, cnt);
     }
 
 #ifdef GIDS_PHASE_TIMERS

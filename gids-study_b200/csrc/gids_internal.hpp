@@ -104,6 +104,7 @@ struct DevCache {
   uint32_t rank;
   uint32_t ref_max;  // clock counter ceiling: 1 = second chance, >1 = frequency clock
   uint32_t pinned_only;  // 1: only permanently pinned lines are inserted; the rest read through
+  uint32_t wb_marks;     // 1: window buffering has marked lines since the pins were last cleared
 };
 
 struct DevBacking {
@@ -267,6 +268,9 @@ class Store {
   int admission = 1;  // 0: insert every miss, 1: insert on the second miss, 2: pinned lines only
   uint32_t ref_max = 3;
   uint64_t refs_since_seen_reset = 0;
+  // window buffering has marked lines since the pins were last cleared: until
+  // then a gather has no window pins to consume and skips reading them
+  bool wb_marked = false;
   void set_policy(int admit, uint32_t ref_ceiling);
   void set_gather_blocks(uint32_t n);
   // gather with the page cache in the library's static no-allocation scratch (noalloc.cu)

@@ -261,6 +261,7 @@ DevCache Store::dev_cache() const {
   c.rank = rank;
   c.ref_max = ref_max;
   c.pinned_only = admission == 2 ? 1u : 0u;
+  c.wb_marks = wb_marked ? 1u : 0u;
   if (admission != 1)
     for (uint32_t r = 0; r < world; r++) c.sh[r].seen = nullptr;
   return c;
@@ -503,6 +504,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   w.n_rows = range_bytes >= w.row_bytes ? (range_bytes - w.row_bytes) / w.stride + 1 : 0;
   w.page_shift = line_shift;
   w.mode = mode;
+  if (mode == WB_MARK) wb_marked = true;  // gathers launched from now on consume window pins
   launch_wb_mark(w, st);
   last_stream = st;
   if (synchronous) GIDS_CUDA(cudaStreamSynchronize(st));
@@ -642,6 +644,7 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
 // its lines from being evicted for good.
 void Store::clear_window_pins() {
   if (d_wb) GIDS_CUDA(cudaMemset(d_wb, 0, (world == 1 ? n_lines : n_lines_local) * sizeof(unsigned int)));
+  wb_marked = false;
 }
 
 void Store::flush_cache() {
