@@ -536,6 +536,64 @@ def parity_check(cfg, ids, feat, hmap, n_rows: int, seed: int = 0) -> dict:
 
 
 # ------------------------------------------------------------------ our arm
+def replica_reservation(args, cfg, sharded: bool) -> int:
+    """Cache lines each shard reserves for replicated rows: up to all of its slots."""
+    if not sharded or args.replicate == "off" or cfg["hetero"]:
+        return 0
+    line = cfg["line"] or cfg["page"]
+    return (cfg["cache_mb"] << 20) // line
+
+
+def replica_model(cum, total: float, per_rank: int, world: int, bw_nvlink: float, bw_host: float,
+                  bw_hbm: float) -> tuple[int, float]:
+    """Rows to replicate and the modelled per-GPU gather rate (GB/s). cum[i] =
+    references to the i hottest rows (cum[0] = 0, len = rows ranked + 1); each
+    GPU holds `per_rank` rows: the R replicated ones and its share of the next
+    world x (per_rank - R), sharded by page id. A reference to a replicated row
+    or to a row of the own shard reads HBM, to another shard NVLink, to an
+    uncached row the host link; per gathered byte the time is the largest of
+    f_remote / BW_NVLink, f_host / BW_host and 2 / BW_HBM (source read and
+    output write), with the link rates at the fractions of their peaks the
+    gather reaches (NVLink 0.86, host link 0.92, HBM 0.85, measured). The
+    smallest R within 0.1 % of the best rate wins."""
+    n = len(cum) - 1
+    best, best_r = 0.0, 0
+    t_hbm = 2.0 / (0.85 * bw_hbm)
+    for r in range(0, per_rank + 1, max(1, per_rank // 64)):
+        a, end = min(r, n), min(r + world * (per_rank - r), n)
+        rep_f = float(cum[a]) / total
+        shard_f = (float(cum[end]) - float(cum[a])) / total
+        remote, host = shard_f * (world - 1) / world, max(0.0, 1.0 - rep_f - shard_f)
+        rate = 1.0 / max(remote / (0.86 * bw_nvlink), host / (0.92 * bw_host), t_hbm)
+        if rate > best * 1.001:
+            best, best_r = rate, r
+    return best_r, best
+
+
+def choose_replicas(args, cfg, g, hot, device, dist, lpr, bw_nvlink, bw_host) -> int:
+    """How many of the hottest rows every rank holds (a prefix of `hot`, the rows
+    in out-degree order). 'auto': replica_model's choice, with the reference
+    counts of 16 minibatches pre-sampled with other seeds and the live link
+    peaks. Every rank uses rank 0's choice."""
+    if args.replicate == "off":
+        return 0
+    per_rank = int(g.BAM_FS.geometry()["cache_slots"]) // lpr
+    if args.replicate != "auto":
+        return int(dist.max(float(min(int(args.replicate), per_rank, hot.numel()))))
+    from GIDS.sampler import out_degree
+
+    counts = torch.zeros(cfg["nodes"], dtype=torch.int32, device=device)
+    for b in batch_stream(cfg, 16, dist.rank + 104729, device):
+        counts += out_degree(b.contiguous(), cfg["nodes"])
+    total = float(counts.sum(dtype=torch.int64))
+    cum = torch.cat([torch.zeros(1, dtype=torch.float64, device=device),
+                     counts[hot].to(torch.float64).cumsum(0)]).cpu()
+    del counts
+    best_r, best = replica_model(cum.numpy(), total, per_rank, g.world, bw_nvlink, bw_host, measured_hbm_peak()[0])
+    log(f"[rank {dist.rank}] replicas: model picks {best_r} rows ({best:.0f} GB/s per GPU modelled)")
+    return int(dist.max(float(best_r))) if dist.rank == 0 else int(dist.max(0.0))
+
+
 def run_ours(args, cfg, dist: Dist):
     import GIDS
 
@@ -580,7 +638,8 @@ def run_ours(args, cfg, dist: Dist):
                   wb_size=max(1, cfg["wb"]), cache_line=cfg["line"] or None,
                   heterograph=cfg["hetero"] is not None, heterograph_map=hmap,
                   cache_admission=POLICIES[args.policy][0], cache_ref_max=POLICIES[args.policy][1],
-                  gather_blocks=args.gather_blocks, wb_prefetch=args.wb_prefetch and cfg["wb"] > 0)
+                  gather_blocks=args.gather_blocks, wb_prefetch=args.wb_prefetch and cfg["wb"] > 0,
+                  replicas=replica_reservation(args, cfg, shared and not args.no_shard))
     t_store = time.time() - t0
     if not shared:
         t0 = time.time()
@@ -609,7 +668,16 @@ def run_ours(args, cfg, dist: Dist):
         g.set_cpu_buffer(pins, int(pins.numel()))
         log(f"[rank {dist.rank}] constant CPU buffer: {pins.numel()} pinned rows (PageRank top "
             f"{cfg['cpu_pin_frac']:.0%})")
+    # link peaks, measured before the static hot set (the replica choice uses them) and reused by the roofline
+    host_peak = host_link_peak_gbs(device, dist)
+    nvlink_peak = None
+    if g.world > 1:
+        # every rank copies 1 GiB from the next rank's shard at the same time
+        dist.barrier()
+        nvlink_peak = g.BAM_FS.peer_copy_gbs((dist.rank + 1) % g.world, 1 << 30)
+        dist.barrier()
     n_static = 0
+    n_replicated = 0
     t_static = 0.0
     if args.policy == "static":
         # the static hot set: the rows neighbour sampling reaches most often (highest out-degree), as many
@@ -638,8 +706,18 @@ def run_ours(args, cfg, dist: Dist):
         else:
             _, indices = graph_csc(cfg, device)
             hot = hot_rows(indices, cfg["nodes"], k)
-        if g.world > 1:  # each rank pins and fills the rows whose first line its shard owns
-            hot = hot[((hot * row_bytes) // line) % g.world == g.rank]
+        if g.world > 1:
+            # replicated rows (the hottest R, held by every rank) take R of each rank's slots; the next
+            # W x (slots - R) rows are sharded by page id, each rank pinning the rows its shard owns
+            n_replicated = 0 if cfg["hetero"] else choose_replicas(args, cfg, g, hot, device, dist, lpr,
+                                                                   nvlink_peak, host_peak)
+            per_rank = geo["cache_slots"] // lpr
+            rest = hot[n_replicated:n_replicated + g.world * (per_rank - n_replicated)]
+            rest = rest[((rest * row_bytes) // line) % g.world == g.rank]
+            if n_replicated:
+                g.replicate_rows(hot[:n_replicated])  # flushes this rank's shard
+            dist.barrier()  # no rank gathers from a shard another rank is still flushing
+            hot = torch.cat([hot[:n_replicated], rest])
         g.pin_cache(hot)  # global row ids (heterograph: no type offset)
         n_static = int(dist.sum(hot.numel()))
         del hot
@@ -690,16 +768,9 @@ def run_ours(args, cfg, dist: Dist):
     bam.reset_stats()
 
     hbm_peak, hbm_src = measured_hbm_peak()
-    host_peak = host_link_peak_gbs(device, dist)
     # the link at the cache's own access size: random line reads from the emulated SSDs
     line_b = int(geo.get("cache_line", page))
     host_rand = bam.host_read_gbs(min(line_b, 4096), 4 << 30)
-    nvlink_peak = None
-    if g.world > 1:
-        # every rank copies 1 GiB from the next rank's shard at the same time
-        dist.barrier()
-        nvlink_peak = bam.peer_copy_gbs((dist.rank + 1) % g.world, 1 << 30)
-        dist.barrier()
 
     # ---- timed region 1: node ids resident in HBM
     clocks = ClockSampler(dist.local)
@@ -875,6 +946,7 @@ def run_ours(args, cfg, dist: Dist):
                      "window_buffer_depth": wb,
                      "cache_policy": args.policy,
                      "static_hot_rows": n_static or None,
+                     "replicated_rows": n_replicated or None,
                      "cache_warmup_minibatches": n_cw,
                      "rank_ms_per_step": rank_ms,
                      "gather_grid_cap": args.gather_blocks or None,
@@ -997,6 +1069,9 @@ def main():
     ap.add_argument("--shared-backing", action="store_true",
                     help="back the emulated SSDs with shared /dev/shm files even on one GPU (as N>1 runs do)")
     ap.add_argument("--gather-blocks", type=int, default=0, help="cap on the gather kernel's grid (0: all resident)")
+    ap.add_argument("--replicate", default="auto",
+                    help="N>1, static policy: rows every rank holds locally besides its shard -- 'off', 'auto' "
+                         "(the count the link model favours) or a row count")
     ap.add_argument("--wb-prefetch", action="store_true",
                     help="window-buffered configs: fetch each batch's lines into the cache as it enters the window")
     ap.add_argument("--cache-warmup", type=int, default=-1,

@@ -100,6 +100,10 @@ class GIDS:
     second-chance clock). Neither changes what is gathered. ``gather_blocks``
     caps the gather kernel's grid (0: every block the GPU holds at once), so a
     gather bound by the host link leaves SMs to kernels on other streams.
+    ``replicas`` (with ``shard_cache``; default 0) reserves room in every
+    shard for that many replicated cache lines: ``replicate_rows`` then makes
+    rows held by every rank in its own shard (their hits are local instead of
+    NVLink reads), while the other rows stay sharded by page id.
     ``wb_prefetch`` (with ``window_buffer``; default False) also fetches into
     the cache, as each batch enters the window, the lines of it that its
     gather would insert (a prefetch launch on the current stream that copies
@@ -112,7 +116,7 @@ class GIDS:
                  ssd_list=None, cache_size=10, ctrl_idx=0, window_buffer=False, wb_size=8, accumulator_flag=False,
                  long_type=False, heterograph=False, heterograph_map=None, *, dtype=None, ssd_capacity=0,
                  ssd_path=None, synchronous=False, shard_cache=False, process_group=None, cache_line=None,
-                 cache_admission=True, cache_ref_max=3, gather_blocks=0, wb_prefetch=False):
+                 cache_admission=True, cache_ref_max=3, gather_blocks=0, wb_prefetch=False, replicas=0):
         if dtype is None:
             dtype = torch.int64 if long_type else torch.float32
         if dtype not in _STORE_CLASSES:
@@ -171,6 +175,9 @@ class GIDS:
                 self.rank = dist.get_rank(process_group)
             if self.world > 1:
                 self.BAM_FS.set_sharding(self.world, self.rank)
+                if replicas:
+                    self.BAM_FS.set_replicas(int(replicas))
+        self.cache_line = int(cache_line or page_size)
         self.BAM_FS.init_controllers(self.GIDS_controller, page_size, self.off, cache_size, num_ele, num_ssd)
         if self.world > 1:
             self._attach_peer_shards()
@@ -288,6 +295,34 @@ class GIDS:
         if self.heterograph:
             return [(self._key_off(k), v) for k, v in batch[0].items()]
         return [(0, batch[0])]
+
+    # ---------------------------------------------------------- replicated rows
+    def _row_lines(self, node_ids, key=None):
+        """Cache lines touched by rows ``node_ids`` (of type ``key``), sorted, unique (int64 CPU)."""
+        ids = torch.as_tensor(node_ids).to(torch.int64).cpu() + (self._key_off(key) if key is not None else 0)
+        esize = torch.empty(0, dtype=self.dtype).element_size()
+        stride = self.cache_dim * esize
+        first = (ids * stride) // self.cache_line
+        last = (ids * stride + stride - 1) // self.cache_line
+        span = int((last - first).max()) + 1 if len(ids) else 1
+        lines = torch.cat([first + k for k in range(span)]) if len(ids) else first
+        if span > 1:
+            lines = lines[lines <= torch.cat([last] * span)]
+        return torch.unique(lines)
+
+    def replicate_rows(self, node_ids, key=None):
+        """Make the cache lines of rows ``node_ids`` replicated (extension): every
+        rank holds them in its own shard, so their hits read local HBM instead
+        of a peer's over NVLink; every other line stays sharded by page id.
+        Collective in effect: every rank replicates the same rows, and no rank
+        gathers until all have (a barrier), since it flushes this rank's shard
+        (call it before ``pin_cache``).
+        At most ``replicas`` lines (the constructor's reservation)."""
+        if self.world <= 1:
+            raise RuntimeError("replicated rows need a sharded cache (shard_cache=True on several ranks)")
+        lines = self._row_lines(node_ids, key).contiguous()
+        self.BAM_FS.set_replicated_lines(lines.data_ptr(), len(lines))
+        return len(lines)
 
     # ---------------------------------------------------------- static hot set
     def pin_cache(self, node_ids, key=None, prefill=True, chunk_rows=1 << 18):

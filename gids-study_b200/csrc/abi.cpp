@@ -245,6 +245,20 @@ int gids_store_set_sharding(gids_store_t* s, int world, int rank) {
   });
 }
 
+int gids_store_set_replicas(gids_store_t* s, uint64_t max_lines) {
+  return guarded([&] {
+    NEED(s);
+    s->s.set_replicas(max_lines);
+  });
+}
+
+int gids_store_set_replicated_lines(gids_store_t* s, const uint64_t* lines, uint64_t n) {
+  return guarded([&] {
+    NEED(s);
+    s->s.set_replicated_lines(lines, n);
+  });
+}
+
 int gids_store_ipc_handle(gids_store_t* s, void* out, size_t len) {
   return guarded([&] {
     NEED(s);

@@ -93,6 +93,7 @@ class FeatureStore {
     int rc = GIDS_OK;
     if (world_ > 1) rc = gids_store_set_sharding(s, world_, rank_);
     if (rc == GIDS_OK && line_) rc = gids_store_set_cache_line(s, line_);
+    if (rc == GIDS_OK && rep_max_) rc = gids_store_set_replicas(s, rep_max_);
     if (rc == GIDS_OK) rc = gids_store_init_controllers(s, ctrl.c, ps, read_off, cache_size, num_ele, num_ssd);
     if (rc != GIDS_OK) {
       char buf[1024];
@@ -196,6 +197,15 @@ class FeatureStore {
     world_ = world;
     rank_ = rank;
   }
+  // replicated lines: entries reserved before init_controllers, then the set
+  // (host int64 array of strictly increasing cache-line ids)
+  void set_replicas(uint64_t max_lines) {
+    if (s_) throw std::runtime_error("gids: set_replicas after init_controllers");
+    rep_max_ = max_lines;
+  }
+  void set_replicated_lines(uint64_t lines_ptr, uint64_t n) {
+    check(gids_store_set_replicated_lines(s(), (const uint64_t*)lines_ptr, n));
+  }
   // cache line in bytes (must be set before init_controllers; 0 = the page)
   void set_cache_line(uint32_t bytes) {
     if (s_) throw std::runtime_error("gids: set_cache_line after init_controllers");
@@ -290,6 +300,7 @@ class FeatureStore {
   int device_ = -1;
   int world_ = 1, rank_ = 0;
   uint32_t line_ = 0;
+  uint64_t rep_max_ = 0;
   uint32_t page_size_ = 0;
   gids_store_t* s_ = nullptr;
   std::vector<uint64_t> offsets_{0, 0, 0};
@@ -348,6 +359,8 @@ void bind_store(py::module_& m, const char* name) {
       // extensions
       .def("set_device", &S::set_device)
       .def("set_sharding", &S::set_sharding, py::arg("world"), py::arg("rank"))
+      .def("set_replicas", &S::set_replicas, py::arg("max_lines"))
+      .def("set_replicated_lines", &S::set_replicated_lines, py::arg("lines_ptr"), py::arg("n"), R())
       .def("set_cache_line", &S::set_cache_line, py::arg("bytes"))
       .def("set_cache_policy", &S::set_cache_policy, py::arg("admission"), py::arg("ref_max"))
       .def("set_gather_blocks", &S::set_gather_blocks, py::arg("max_blocks"))

@@ -515,7 +515,6 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
   const uint32_t shift = a.c.page_shift;
   const uint64_t psize = a.c.page_size;
   const bool have_cache = a.c.n_slots != 0;
-  const uint32_t world = a.c.world;
   const uint64_t n_warps = (uint64_t)gridDim.x * WARPS;
 
   int ti = 0;
@@ -563,8 +562,13 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       const uint64_t pe = pb + psize, re = b0 + a.row_bytes;
       s1 = (uint32_t)((pe < re ? pe : re) - b0);
     }
-    const uint32_t owner = (SYS && seg_ok) ? (uint32_t)(p % world) : 0u;
-    const uint64_t lp = SYS ? p / world : p;  // index in the owner's page table
+    uint32_t owner = 0u;
+    uint64_t lp = p;  // index in the owner's page table
+    if (SYS) {
+      const LineHome h = line_home(a.c, seg_ok ? p : 0ull);
+      owner = seg_ok ? h.owner : 0u;
+      lp = h.entry;
+    }
     const DevShard& S = a.c.sh[owner];
 
     // ---- 2. warp dedup + acquire (one leader per distinct page)
@@ -987,7 +991,11 @@ __global__ void wb_mark_kernel(const __grid_constant__ WbArgs a) {
   const uint64_t b0 = (uint64_t)rs * a.stride;
   const uint64_t p0 = b0 >> a.page_shift, p1 = (b0 + a.row_bytes - 1) >> a.page_shift;
   for (uint64_t p = p0; p <= p1; p++) {
-    unsigned int* const w = a.world == 1 ? a.wb[0] + p : a.wb[p % a.world] + p / a.world;
+    unsigned int* w = a.wb[0] + p;
+    if (a.world > 1) {
+      const LineHome h = line_home(a.home, p);
+      w = a.wb[h.owner] + h.entry;
+    }
     switch (a.mode) {
       case WB_MARK:
         if (a.world == 1)

@@ -105,7 +105,37 @@ struct DevCache {
   uint32_t ref_max;  // clock counter ceiling: 1 = second chance, >1 = frequency clock
   uint32_t pinned_only;  // 1: only permanently pinned lines are inserted; the rest read through
   uint32_t wb_marks;     // 1: window buffering has marked lines since the pins were last cleared
+  // Replicated lines (sharded caches): a line whose bit is set is held by
+  // every rank, in its own shard, at page-table entry n_local + (its rank
+  // among the set bits); every other line is owned by rank line % world.
+  const unsigned long long* rep_bits;  // [rep_words] one bit per line, or nullptr
+  const unsigned int* rep_rank;        // [rep_words] set bits in the words before
+  uint64_t rep_words;
+  uint64_t n_local;  // page-table entries of the lines a shard owns; replicas follow
 };
+
+// Shard and page-table entry of cache line p: its owner's shard at p / world,
+// or, for a replicated line, this rank's own shard after the owned entries.
+#ifdef __CUDACC__
+struct LineHome {
+  uint32_t owner;
+  uint64_t entry;
+};
+__device__ __forceinline__ LineHome line_home(const DevCache& c, uint64_t p) {
+  LineHome h{(uint32_t)(p % c.world), p / c.world};
+  if (c.rep_bits) {
+    const uint64_t w = p >> 6;
+    if (w < c.rep_words) {
+      const unsigned long long bits = __ldg(c.rep_bits + w);
+      if ((bits >> (p & 63)) & 1ull) {
+        h.owner = c.rank;
+        h.entry = c.n_local + (uint64_t)__ldg(c.rep_rank + w) + (uint64_t)__popcll(bits & ((1ull << (p & 63)) - 1ull));
+      }
+    }
+  }
+  return h;
+}
+#endif
 
 struct DevBacking {
   const char* ssd[GIDS_MAX_SSD];  // device addresses of the mapped SSD regions
@@ -155,6 +185,7 @@ struct GatherArgs {
 struct WbArgs {
   unsigned int* wb[GIDS_MAX_WORLD];  // pin counters of every shard
   uint32_t world;
+  DevCache home;  // line -> (shard, entry) when sharded (line_home); only its rep/rank/world fields are used
   const int64_t* idx;
   uint64_t n;
   int64_t off;
@@ -297,6 +328,16 @@ class Store {
   uint32_t line_request = 0;                // set_cache_line before init; 0 = the page
   uint64_t read_off_pages = 0, num_ele = 0, range_bytes = 0, n_pages = 0, n_slots = 0;
   uint64_t n_lines = 0, n_lines_local = 0;
+  // replicated lines (sharded caches): page-table entries reserved after the
+  // owned ones (set_replicas, before init_controllers; the same on every
+  // rank), the lines now replicated, and their bitmap and rank words
+  uint64_t n_rep_max = 0, n_rep = 0, rep_words = 0;
+  unsigned long long* d_rep_bits = nullptr;
+  unsigned int* d_rep_rank = nullptr;
+  uint64_t n_entries_local() const { return n_lines_local + n_rep_max; }
+  void set_replicas(uint64_t max_lines);
+  // host array of cache-line ids, strictly increasing; flushes this rank's shard
+  void set_replicated_lines(const uint64_t* lines, uint64_t n);
   uint32_t row_layout = 0;  // source row stride (elements) for CPU-buffer fills / WB; 0 = unknown
 
   // sharding (page p is owned by rank p % world)

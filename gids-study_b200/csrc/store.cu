@@ -93,6 +93,9 @@ void Store::free_all() {
   d_slots = nullptr;
   f(d_cpu_bits);
   f(d_cpu_rank);
+  f(d_rep_bits);
+  f(d_rep_rank);
+  n_rep = rep_words = 0;
   cpu_buf.release();
 }
 
@@ -131,6 +134,53 @@ struct ShardLayout {
 };
 }  // namespace
 
+void Store::set_replicas(uint64_t max_lines) {
+  std::lock_guard<std::mutex> lk(mu);
+  GIDS_CHECK(!initialized, GIDS_E_STATE, "set_replicas after init_controllers");
+  GIDS_CHECK(max_lines < (1ull << 32), GIDS_E_INVAL, "at most 2^32 - 1 replicated lines");
+  n_rep_max = max_lines;
+}
+
+// The lines every rank holds in its own shard: a bitmap over the range's lines
+// and, per 64-bit word, the number of set bits before it (built on the host,
+// once; the kernels find a line's entry with one word load and a popcount).
+// The replica entries are cleared with the rest of this rank's shard, so that
+// no slot stays tagged with an entry that now means another line.
+void Store::set_replicated_lines(const uint64_t* lines, uint64_t n) {
+  GIDS_CHECK(initialized, GIDS_E_STATE, "set_replicated_lines before init_controllers");
+  GIDS_CHECK(world > 1, GIDS_E_STATE, "replicated lines need a sharded cache");
+  GIDS_CHECK(n <= n_rep_max, GIDS_E_RANGE, "more replicated lines than set_replicas reserved");
+  GIDS_CHECK(n == 0 || lines, GIDS_E_INVAL, "null line array");
+  for (uint64_t i = 0; i < n; i++) {
+    GIDS_CHECK(lines[i] < n_lines, GIDS_E_RANGE, "replicated line outside the range");
+    GIDS_CHECK(i == 0 || lines[i] > lines[i - 1], GIDS_E_INVAL, "replicated lines must be strictly increasing");
+  }
+  flush_cache();
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceGuard g(device);
+  if (d_rep_bits) GIDS_CUDA(cudaFree(d_rep_bits));
+  if (d_rep_rank) GIDS_CUDA(cudaFree(d_rep_rank));
+  d_rep_bits = nullptr;
+  d_rep_rank = nullptr;
+  n_rep = rep_words = 0;
+  if (!n) return;
+  const uint64_t words = (lines[n - 1] >> 6) + 1;
+  std::vector<unsigned long long> bits(words, 0ull);
+  std::vector<unsigned int> rank_words(words, 0u);
+  for (uint64_t i = 0; i < n; i++) bits[lines[i] >> 6] |= 1ull << (lines[i] & 63);
+  uint64_t before = 0;
+  for (uint64_t w = 0; w < words; w++) {
+    rank_words[w] = (unsigned int)before;
+    before += (uint64_t)__builtin_popcountll(bits[w]);
+  }
+  GIDS_CUDA(cudaMalloc(&d_rep_bits, words * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMalloc(&d_rep_rank, words * sizeof(unsigned int)));
+  GIDS_CUDA(cudaMemcpy(d_rep_bits, bits.data(), words * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+  GIDS_CUDA(cudaMemcpy(d_rep_rank, rank_words.data(), words * sizeof(unsigned int), cudaMemcpyHostToDevice));
+  n_rep = n;
+  rep_words = words;
+}
+
 void Store::set_sharding(uint32_t w, uint32_t r) {
   std::lock_guard<std::mutex> lk(mu);
   GIDS_CHECK(!initialized, GIDS_E_STATE, "set_sharding after init_controllers");
@@ -153,7 +203,7 @@ void Store::open_peers(const void* handles, uint32_t n) {
   GIDS_CHECK(initialized, GIDS_E_STATE, "open_peers before init_controllers");
   GIDS_CHECK(n == world, GIDS_E_INVAL, "need one handle per rank");
   DeviceGuard g(device);
-  const ShardLayout L(n_lines_local, n_slots, line_size, world > 1);
+  const ShardLayout L(n_entries_local(), n_slots, line_size, world > 1);
   const cudaIpcMemHandle_t* h = (const cudaIpcMemHandle_t*)handles;
   for (uint32_t r = 0; r < world; r++) {
     if (r == rank) continue;
@@ -172,7 +222,7 @@ void Store::share_in_process(Store* const* stores, uint32_t n) {
     GIDS_CHECK(s && s->initialized, GIDS_E_STATE, "every store must be initialised");
     GIDS_CHECK(s->world == n && s->rank == i, GIDS_E_INVAL, "store i must have world n and rank i");
     GIDS_CHECK(s->n_lines == stores[0]->n_lines && s->n_slots == stores[0]->n_slots &&
-                   s->line_size == stores[0]->line_size,
+                   s->line_size == stores[0]->line_size && s->n_rep_max == stores[0]->n_rep_max,
                GIDS_E_INVAL, "stores differ in geometry");
   }
   for (uint32_t i = 0; i < n; i++)
@@ -225,8 +275,9 @@ void Store::init_controllers(Controllers* c, uint32_t ps, uint64_t read_off_page
   // this rank's shard: page table of the pages it owns (p % world == rank),
   // slots, clock and (when sharded) window-buffer pins, in one allocation
   n_lines_local = (n_lines + world - 1) / world;
+  if (world == 1) n_rep_max = 0;  // replicas only make sense in a sharded cache
   const bool with_wb = world > 1;
-  const ShardLayout L(n_lines_local, n_slots, line_size, with_wb);
+  const ShardLayout L(n_entries_local(), n_slots, line_size, with_wb);
   shard_bytes = L.total;
   GIDS_CUDA(cudaMalloc(&d_shard, shard_bytes));
   const DevShard mine = L.at(d_shard, with_wb);
@@ -262,6 +313,12 @@ DevCache Store::dev_cache() const {
   c.ref_max = ref_max;
   c.pinned_only = admission == 2 ? 1u : 0u;
   c.wb_marks = wb_marked ? 1u : 0u;
+  c.n_local = n_lines_local;
+  if (n_rep) {
+    c.rep_bits = d_rep_bits;
+    c.rep_rank = d_rep_rank;
+    c.rep_words = rep_words;
+  }
   if (admission != 1)
     for (uint32_t r = 0; r < world; r++) c.sh[r].seen = nullptr;
   return c;
@@ -419,7 +476,7 @@ void Store::read_multi(int k, void* const* outs, const int64_t* const* idxs, con
     for (int i = 0; i < k; i++) refs += ns[i] * max_pages;
     refs_since_seen_reset += refs;
     if (refs_since_seen_reset > 2 * n_slots) {
-      const ShardLayout Ls(n_lines_local, n_slots, line_size, world > 1);
+      const ShardLayout Ls(n_entries_local(), n_slots, line_size, world > 1);
       GIDS_CUDA(cudaMemsetAsync(d_shard + Ls.seen, 0, Ls.seen_bytes, st));
       refs_since_seen_reset = refs;
     }
@@ -495,6 +552,7 @@ void Store::window_buffering(const int64_t* idx, int64_t n, int64_t off, uint32_
   uint32_t se = stride_elems ? stride_elems : row_layout ? row_layout : page_size / elem_bytes;
   WbArgs w{};
   w.world = world;
+  w.home = dev_cache();
   for (uint32_t r = 0; r < world; r++) w.wb[r] = world == 1 ? d_wb : shards[r].wb;
   w.idx = idx;
   w.n = (uint64_t)n;
@@ -629,7 +687,7 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
   }
   // the cache and the CPU buffer may hold stale copies of the written pages
   // (a sharded cache drops this rank's shard; every rank has to flush)
-  GIDS_CUDA(cudaMemset(d_state, 0, n_lines_local * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_state, 0, n_entries_local() * sizeof(unsigned long long)));
   if (n_slots) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
@@ -643,7 +701,7 @@ void Store::write_range(const void* src, uint64_t nbytes, uint64_t off) {
 // unsharded). A marked window that is never gathered would otherwise keep
 // its lines from being evicted for good.
 void Store::clear_window_pins() {
-  if (d_wb) GIDS_CUDA(cudaMemset(d_wb, 0, (world == 1 ? n_lines : n_lines_local) * sizeof(unsigned int)));
+  if (d_wb) GIDS_CUDA(cudaMemset(d_wb, 0, (world == 1 ? n_lines : n_entries_local()) * sizeof(unsigned int)));
   wb_marked = false;
 }
 
@@ -656,14 +714,14 @@ void Store::flush_cache() {
   GIDS_CHECK(initialized, GIDS_E_STATE, "flush_cache before init_controllers");
   DeviceGuard g(device);
   GIDS_CUDA(cudaDeviceSynchronize());
-  GIDS_CUDA(cudaMemset(d_state, 0, n_lines_local * sizeof(unsigned long long)));
+  GIDS_CUDA(cudaMemset(d_state, 0, n_entries_local() * sizeof(unsigned long long)));
   if (n_slots) {
     GIDS_CUDA(cudaMemset(d_slot_page, 0xFF, n_slots * sizeof(unsigned long long)));
     GIDS_CUDA(cudaMemset(d_slot_ref, 0, n_slots));
   }
   // and forget which lines missed once; the clock restarts, so the empty
   // cache admits every miss again
-  const ShardLayout L(n_lines_local, n_slots, line_size, world > 1);
+  const ShardLayout L(n_entries_local(), n_slots, line_size, world > 1);
   GIDS_CUDA(cudaMemset(d_shard + L.seen, 0, L.seen_bytes));
   GIDS_CUDA(cudaMemset(d_shard + L.clock, 0, 8));
   clear_window_pins();

@@ -168,6 +168,17 @@ GIDS_API int gids_store_set_row_layout(gids_store_t *s, uint32_t cache_dim);
  * shard must outlive every gather of every rank (destroy after a barrier);
  * flush_cache and writes drop only the calling rank's shard. */
 GIDS_API int gids_store_set_sharding(gids_store_t *s, int world, int rank);
+/* Replicated lines (no reference counterpart): in a sharded cache, lines
+ * that every rank holds in its own shard instead of only their owner's, so
+ * that hits on them are local rather than NVLink reads. set_replicas reserves
+ * page-table entries for up to max_lines of them (before init_controllers,
+ * the same on every rank; < 2^32). set_replicated_lines makes `lines` (a host
+ * array of cache-line ids, strictly increasing, at most max_lines) the
+ * replicated set of the calling rank and flushes that rank's shard; every rank
+ * must set the same lines before gathering. Pins (gids_store_pin_rows) of a
+ * replicated line pin this rank's copy. */
+GIDS_API int gids_store_set_replicas(gids_store_t *s, uint64_t max_lines);
+GIDS_API int gids_store_set_replicated_lines(gids_store_t *s, const uint64_t *lines, uint64_t n);
 GIDS_API int gids_store_ipc_handle(gids_store_t *s, void *out, size_t len);
 GIDS_API int gids_store_open_peers(gids_store_t *s, const void *handles, int world);
 GIDS_API int gids_store_share_shards(gids_store_t *const *stores, int n);

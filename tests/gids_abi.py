@@ -52,6 +52,8 @@ def lib():
             "gids_read_feature_multi": (i32, [vp, i32, P(vp), P(vp), P(u64), i32, i32, P(u64), vp]),
             "gids_read_feature_noalloc": (i32, [vp, vp, vp, i64, i32, i32, u64, vp]),
             "gids_prefetch": (i32, [vp, vp, i64, i32, i32, u64, vp]),
+            "gids_store_set_replicas": (i32, [vp, u64]),
+            "gids_store_set_replicated_lines": (i32, [vp, vp, u64]),
             "gids_set_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_unset_window_buffering": (i32, [vp, vp, i64, i64, u32, vp]),
             "gids_store_pin_rows": (i32, [vp, vp, i64, i64, u32, vp]),

@@ -205,6 +205,42 @@ def test_window_buffer_prefetch_follows_each_mark(fake):
     assert not [c for c in g2.BAM_FS.calls if c[0] == "prefetch"]
 
 
+def test_replicated_rows_map_to_their_cache_lines(fake):
+    g = fake()  # float32 x 64 columns: 256-byte rows, 4 KB lines
+    assert g._row_lines(torch.tensor([0, 15, 16, 100, 16])).tolist() == [0, 1, 6]
+    g.cache_dim = 768  # 3072-byte rows straddle 4 KB lines
+    assert g._row_lines(torch.tensor([1, 0, 3])).tolist() == [0, 1, 2]  # row 3 is bytes 9216-12287: line 2
+    assert g._row_lines(torch.tensor([2])).tolist() == [1, 2]
+    with pytest.raises(RuntimeError):
+        g.replicate_rows(torch.tensor([1]))  # one rank: no sharded cache to replicate in
+
+
+def test_replica_model_trades_nvlink_for_host_reads():
+    import bench
+
+    ranked = 8000
+    refs = 1.0 / np.arange(1, ranked + 1)  # Zipf-like reference counts, hottest first
+    cum = np.concatenate([[0.0], np.cumsum(refs)])
+    total = float(cum[-1]) * 1.004  # 0.4 % of the references go to rows beyond the ranked ones
+    # 8 GPUs of 1000 rows each hold all 8000 ranked rows unreplicated: NVLink-bound
+    r8, rate8 = bench.replica_model(cum, total, 1000, 8, 737.0, 25.0, 6559.0)
+    r0 = bench.replica_model(cum, total, 1000, 8, 737.0, 25.0, 6559.0)  # deterministic
+    assert (r8, rate8) == r0 and r8 > 0
+    # the rate at R = r8 beats R = 0: compare with a model that may not replicate
+    _, rate_no = bench.replica_model(cum, total, 0, 8, 737.0, 25.0, 6559.0)
+    assert rate8 > rate_no
+    # a slow host link makes host reads dear: fewer rows replicated
+    r_slow, _ = bench.replica_model(cum, total, 1000, 8, 737.0, 2.0, 6559.0)
+    assert r_slow < r8
+    # 2 GPUs of 1000 rows: 6000 ranked rows are read from the host already; replicating adds more: none
+    r2, _ = bench.replica_model(cum, total, 1000, 2, 737.0, 25.0, 6559.0)
+    assert r2 == 0
+    # everything cached and a fast host link: replicate until the HBM term binds, no further
+    cum_all = np.concatenate([[0.0], np.cumsum(refs[:2000])])
+    r_all, rate_all = bench.replica_model(cum_all, float(cum_all[-1]), 1000, 2, 737.0, 1e9, 6559.0)
+    assert 0 < r_all < 1000 and abs(rate_all - 0.85 * 6559.0 / 2) < 1.0
+
+
 def test_accumulator_merges_until_threshold(fake):
     g = fake(accumulator_flag=True)
     g.set_required_storage_access(bw=1.0, l_ssd=10, l_system=5, num_ssd=1, p=0.5)

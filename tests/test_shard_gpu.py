@@ -30,7 +30,7 @@ def bits_equal(a: torch.Tensor, b: np.ndarray) -> bool:
 class Shared:
     """Controllers + `world` stores on one device, shards shared in-process."""
 
-    def __init__(self, table, world, page=4096, cache_mb=1, num_ssd=2, device=0, line=0, admission=True):
+    def __init__(self, table, world, page=4096, cache_mb=1, num_ssd=2, device=0, line=0, admission=True, replicas=0):
         L = gids_abi.lib()
         self.c = ctypes.c_void_p()
         check(L.gids_ctrls_create(ctypes.byref(self.c)))
@@ -45,6 +45,8 @@ class Shared:
             check(L.gids_store_set_sharding(s, world, r))
             if line:
                 check(L.gids_store_set_cache_line(s, line))
+            if replicas:
+                check(L.gids_store_set_replicas(s, replicas))
             check(L.gids_store_init_controllers(s, self.c, page, 0, cache_mb, table.size, num_ssd))
             check(L.gids_store_set_cache_policy(s, 1 if admission else 0, 3))
             self.s.append(s)
@@ -147,6 +149,90 @@ def test_in_process_shards_prefetch(world):
             assert st["miss"] == 0 and st["bypass"] == 0 and st["hit"] == st["access"]
     finally:
         sh.close()
+
+
+def _replicate(sh, lines):
+    arr = np.ascontiguousarray(np.asarray(lines, dtype=np.uint64))
+    for s in sh.s:
+        check(gids_abi.lib().gids_store_set_replicated_lines(s, arr.ctypes.data, len(arr)))
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_in_process_shards_replicated_lines(world):
+    """Replicated lines live in every rank's own shard: their hits are local,
+    each rank fills its own copy, and every gather stays bit-exact."""
+    rows, cdim = 6000, 1024  # 4 KB rows: row i is line i
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 29, rows, cdim)
+    sh = Shared(t, world, cache_mb=64, admission=False, replicas=1000)
+    rng = np.random.default_rng(world + 20)
+    L = gids_abi.lib()
+    try:
+        rep_lines = np.sort(rng.choice(rows, size=700, replace=False))
+        _replicate(sh, rep_lines)
+        ids = np.concatenate([rep_lines, rng.choice(rep_lines, size=1300)])
+        rng.shuffle(ids)
+        for r in range(world):  # every rank fills its own copies, then hits them
+            check(L.gids_reset_stats(sh.s[r]))
+            assert bits_equal(sh.gather(r, ids, cdim, cdim), oracle.gather(t, ids))
+            st = sh.stats(r)
+            assert st["bytes_peer"] == 0 and st["read_io"] == len(np.unique(ids)) and st["bypass"] == 0
+            check(L.gids_reset_stats(sh.s[r]))
+            assert bits_equal(sh.gather(r, ids[::-1].copy(), cdim, cdim), oracle.gather(t, ids[::-1]))
+            st = sh.stats(r)
+            assert st["hit"] == st["access"] and st["bytes_peer"] == 0
+        # the other lines stay sharded by page id: hits on them come from the owners
+        other = np.setdiff1d(np.arange(rows), rep_lines)
+        ids2 = rng.choice(other, size=3000)
+        mixed = np.concatenate([ids2, rng.choice(rep_lines, size=500)])
+        rng.shuffle(mixed)
+        for r in range(world):
+            check(L.gids_reset_stats(sh.s[r]))
+            assert bits_equal(sh.gather(r, mixed, cdim, cdim), oracle.gather(t, mixed))
+        st = sh.stats(world - 1)  # by now every line is resident: a sharded hit off-rank is a peer read
+        assert st["hit"] == st["access"] and st["bytes_peer"] > 0
+        # the replica entries follow the owned ones: a set larger than reserved, or unsorted, is refused
+        big = np.arange(1001, dtype=np.uint64)
+        assert L.gids_store_set_replicated_lines(sh.s[0], big.ctypes.data, len(big)) == gids_abi.GIDS_E_RANGE
+        bad = np.array([5, 3], dtype=np.uint64)
+        assert L.gids_store_set_replicated_lines(sh.s[0], bad.ctypes.data, 2) == gids_abi.GIDS_E_INVAL
+    finally:
+        sh.close()
+
+
+def test_replicated_lines_pinned_under_static_policy():
+    """Pins of replicated rows pin each rank's own copy; the static policy then
+    holds them locally on every rank."""
+    rows, cdim, world = 4000, 1024, 2
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 30, rows, cdim)
+    sh = Shared(t, world, cache_mb=8, admission=False, replicas=256)  # 2048 slots per shard
+    L = gids_abi.lib()
+    try:
+        hot = np.arange(100, 356)  # 256 rows, replicated
+        _replicate(sh, hot)
+        d = torch.as_tensor(hot, dtype=torch.int64).cuda()
+        for r in range(world):
+            check(L.gids_store_set_cache_policy(sh.s[r], 2, 3))
+            check(L.gids_store_pin_rows(sh.s[r], ctypes.c_void_p(d.data_ptr()), len(hot), 0, 0, None))
+        torch.cuda.synchronize()
+        for r in range(world):
+            sh.gather(r, hot, cdim, cdim)  # fills the pinned copies
+            check(L.gids_reset_stats(sh.s[r]))
+            out = sh.gather(r, np.concatenate([hot, np.arange(2000, 2100)]), cdim, cdim)
+            assert bits_equal(out, oracle.gather(t, np.concatenate([hot, np.arange(2000, 2100)])))
+            st = sh.stats(r)
+            assert st["hit"] == 256 and st["bypass"] == 100 and st["bytes_peer"] == 0
+    finally:
+        sh.close()
+
+
+def test_replicas_need_a_sharded_cache():
+    t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 1, 100, 256)
+    s = gids_abi.Store(4, 4096, t.size, 1)
+    try:
+        one = np.array([1], dtype=np.uint64)
+        assert gids_abi.lib().gids_store_set_replicated_lines(s.s, one.ctypes.data, 1) == gids_abi.GIDS_E_STATE
+    finally:
+        s.close()
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
