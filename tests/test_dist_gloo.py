@@ -60,10 +60,13 @@ def _worker(rank, world, port, q):
 
         gmod._feature_store_module = lambda: types.SimpleNamespace(BAM_Feature_Store_float=FakeStore,
                                                                    GIDS_Controllers=FakeCtrl)
-        g = gmod.GIDS(page_size=4096, cache_dim=64, num_ele=1000 * 64, shard_cache=True)
+        g = gmod.GIDS(page_size=4096, cache_dim=64, num_ele=1000 * 64, shard_cache=True, replicas=100)
+        n_rep = g.replicate_rows(torch.tensor([0, 16, 17, 5]))  # 256-byte rows: lines 0 and 1
         names = [c[0] for c in g.BAM_FS.calls]
         opened = [c for c in g.BAM_FS.calls if c[0] == "open_peers"][0][1]
-        q.put((rank, t_max, s_sum, bench.sampler_seed(rank), g.world, g.rank, names, opened, per_rank))
+        rep_call = [c for c in g.BAM_FS.calls if c[0] == "set_replicated_lines"][0]
+        q.put((rank, t_max, s_sum, bench.sampler_seed(rank), g.world, g.rank, names, opened, per_rank,
+               (n_rep, rep_call[2], ("set_replicas", 100) in g.BAM_FS.calls)))
         d.close()
     except Exception as e:
         q.put((rank, "error", repr(e)))
@@ -88,7 +91,7 @@ def test_two_ranks_gloo():
                 p.kill()
     for r in (0, 1):
         assert out[r][1] != "error", out[r]
-        _, t_max, s_sum, seed, world, grank, names, opened, per_rank = out[r]
+        _, t_max, s_sum, seed, world, grank, names, opened, per_rank, reps = out[r]
         assert t_max == 2.0 and s_sum == 30.0  # max and sum over both ranks
         assert per_rank == [0.5, 1.5]  # every rank's value, in rank order
         assert seed == 1000 + r
@@ -96,3 +99,6 @@ def test_two_ranks_gloo():
         # sharding is set before init_controllers; handles arrive in rank order
         assert names.index("set_sharding") < names.index("init_controllers") < names.index("open_peers")
         assert opened == [bytes([0]) * 64, bytes([1]) * 64]
+        # replicas are reserved before the shard exists; two distinct lines are replicated
+        assert names.index("set_sharding") < names.index("set_replicas") < names.index("init_controllers")
+        assert reps == (2, 2, True)
