@@ -195,9 +195,14 @@ class GIDS:
         """Exchange the shards' CUDA IPC handles and map every peer's shard."""
         import torch.distributed as dist
 
-        handles = [None] * self.world
-        dist.all_gather_object(handles, self.BAM_FS.ipc_handle(), group=self._pg)
-        self.BAM_FS.open_peers(handles)
+        mine = (self.BAM_FS.ipc_handle(), int(self.BAM_FS.geometry().get("shard_bytes", 0)))
+        got = [None] * self.world
+        dist.all_gather_object(got, mine, group=self._pg)
+        # a peer's shard is addressed by this rank's layout: the ranks' shards must be alike
+        if len({b for _, b in got}) != 1:
+            raise RuntimeError(f"sharded cache: the ranks' shards differ in size ({[b for _, b in got]}); "
+                               "every rank needs the same geometry, cache line and replicas")
+        self.BAM_FS.open_peers([h for h, _ in got])
         dist.barrier(group=self._pg)
 
     def close(self):

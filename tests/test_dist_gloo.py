@@ -56,6 +56,9 @@ def _worker(rank, world, port, q):
             def open_peers(self, handles):
                 self.calls.append(("open_peers", list(handles)))
 
+            def geometry(self):
+                return {"shard_bytes": 1 << 21}
+
         import types
 
         gmod._feature_store_module = lambda: types.SimpleNamespace(BAM_Feature_Store_float=FakeStore,
