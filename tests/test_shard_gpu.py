@@ -225,6 +225,37 @@ def test_replicated_lines_pinned_under_static_policy():
         sh.close()
 
 
+def test_replicated_rows_straddling_small_lines():
+    """fp16 rows of 1536 bytes over 512-byte lines: a replicated row's three lines
+    are all local; rows sharing a line with a replicated row stay exact."""
+    rows, cdim, world = 5000, 768, 2
+    t = oracle.synth_table(oracle.KIND_F16_NORMAL, 31, rows, cdim)
+    sh = Shared(t, world, cache_mb=16, line=512, admission=False, replicas=4000)
+    L = gids_abi.lib()
+    try:
+        rng = np.random.default_rng(33)
+        rep_rows = np.sort(rng.choice(rows, size=900, replace=False))
+        stride = cdim * 2
+        lines = np.unique(np.concatenate([(rep_rows * stride + k * 512) // 512 for k in range(3)]))
+        _replicate(sh, lines)
+        for r in range(world):
+            d = torch.as_tensor(rep_rows, dtype=torch.int64).cuda()
+            out = torch.empty((len(rep_rows), cdim), device="cuda", dtype=torch.float16)
+            check(L.gids_reset_stats(sh.s[r]))
+            check(L.gids_read_feature(sh.s[r], out.data_ptr(), d.data_ptr(), len(rep_rows), cdim, cdim, 0, None))
+            torch.cuda.synchronize()
+            assert bits_equal(out, oracle.gather(t, rep_rows))
+            assert sh.stats(r)["bytes_peer"] == 0
+            mixed = rng.integers(0, rows, size=3000)
+            dm = torch.as_tensor(mixed, dtype=torch.int64).cuda()
+            out = torch.empty((len(mixed), cdim), device="cuda", dtype=torch.float16)
+            check(L.gids_read_feature(sh.s[r], out.data_ptr(), dm.data_ptr(), len(mixed), cdim, cdim, 0, None))
+            torch.cuda.synchronize()
+            assert bits_equal(out, oracle.gather(t, mixed))
+    finally:
+        sh.close()
+
+
 def test_replicas_need_a_sharded_cache():
     t = oracle.synth_table(oracle.KIND_F32_UNIFORM, 1, 100, 256)
     s = gids_abi.Store(4, 4096, t.size, 1)
