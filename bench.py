@@ -544,27 +544,28 @@ def replica_reservation(args, cfg, sharded: bool) -> int:
     return (cfg["cache_mb"] << 20) // line
 
 
-def replica_model(cum, total: float, per_rank: int, world: int, bw_nvlink: float, bw_host: float,
-                  bw_hbm: float) -> tuple[int, float]:
+def replica_model(cum, total: float, per_rank: int, world: int, bw_nvlink: float,
+                  bw_host: float) -> tuple[int, float]:
     """Rows to replicate and the modelled per-GPU gather rate (GB/s). cum[i] =
     references to the i hottest rows (cum[0] = 0, len = rows ranked + 1); each
     GPU holds `per_rank` rows: the R replicated ones and its share of the next
     world x (per_rank - R), sharded by page id. A reference to a replicated row
     or to a row of the own shard reads HBM, to another shard NVLink, to an
-    uncached row the host link; per gathered byte the time is the largest of
-    f_remote / BW_NVLink, f_host / BW_host and 2 / BW_HBM (source read and
-    output write), with the link rates at the fractions of their peaks the
-    gather reaches (NVLink 0.86, host link 0.92, HBM 0.85, measured). The
-    smallest R within 0.1 % of the best rate wins."""
+    uncached row the host link; per gathered byte the time is the larger of
+    f_remote / BW_NVLink and f_host / BW_host, with the link rates at the
+    fractions of their peaks the gather reaches (NVLink 0.86, host link 0.92,
+    measured). HBM is left out: replication moves no HBM traffic (every cached
+    byte is read from some GPU's HBM either way), and on 2 GPUs a model capped
+    by an HBM term stopped short of the measured best. The smallest R within
+    0.1 % of the best rate wins."""
     n = len(cum) - 1
     best, best_r = 0.0, 0
-    t_hbm = 2.0 / (0.85 * bw_hbm)
     for r in range(0, per_rank + 1, max(1, per_rank // 64)):
         a, end = min(r, n), min(r + world * (per_rank - r), n)
         rep_f = float(cum[a]) / total
         shard_f = (float(cum[end]) - float(cum[a])) / total
         remote, host = shard_f * (world - 1) / world, max(0.0, 1.0 - rep_f - shard_f)
-        rate = 1.0 / max(remote / (0.86 * bw_nvlink), host / (0.92 * bw_host), t_hbm)
+        rate = 1.0 / max(remote / (0.86 * bw_nvlink), host / (0.92 * bw_host), 1e-9)
         if rate > best * 1.001:
             best, best_r = rate, r
     return best_r, best
@@ -589,7 +590,7 @@ def choose_replicas(args, cfg, g, hot, device, dist, lpr, bw_nvlink, bw_host) ->
     cum = torch.cat([torch.zeros(1, dtype=torch.float64, device=device),
                      counts[hot].to(torch.float64).cumsum(0)]).cpu()
     del counts
-    best_r, best = replica_model(cum.numpy(), total, per_rank, g.world, bw_nvlink, bw_host, measured_hbm_peak()[0])
+    best_r, best = replica_model(cum.numpy(), total, per_rank, g.world, bw_nvlink, bw_host)
     log(f"[rank {dist.rank}] replicas: model picks {best_r} rows ({best:.0f} GB/s per GPU modelled)")
     return int(dist.max(float(best_r))) if dist.rank == 0 else int(dist.max(0.0))
 

@@ -223,22 +223,23 @@ def test_replica_model_trades_nvlink_for_host_reads():
     cum = np.concatenate([[0.0], np.cumsum(refs)])
     total = float(cum[-1]) * 1.004  # 0.4 % of the references go to rows beyond the ranked ones
     # 8 GPUs of 1000 rows each hold all 8000 ranked rows unreplicated: NVLink-bound
-    r8, rate8 = bench.replica_model(cum, total, 1000, 8, 737.0, 25.0, 6559.0)
-    r0 = bench.replica_model(cum, total, 1000, 8, 737.0, 25.0, 6559.0)  # deterministic
+    r8, rate8 = bench.replica_model(cum, total, 1000, 8, 737.0, 25.0)
+    r0 = bench.replica_model(cum, total, 1000, 8, 737.0, 25.0)  # deterministic
     assert (r8, rate8) == r0 and r8 > 0
-    # the rate at R = r8 beats R = 0: compare with a model that may not replicate
-    _, rate_no = bench.replica_model(cum, total, 0, 8, 737.0, 25.0, 6559.0)
+    # the rate at R = r8 beats the rate without replicas (all 8000 rows sharded)
+    cached = cum[-1] / total
+    rate_no = 1.0 / max(cached * 7 / 8 / (0.86 * 737.0), (1 - cached) / (0.92 * 25.0))
     assert rate8 > rate_no
     # a slow host link makes host reads dear: fewer rows replicated
-    r_slow, _ = bench.replica_model(cum, total, 1000, 8, 737.0, 2.0, 6559.0)
+    r_slow, _ = bench.replica_model(cum, total, 1000, 8, 737.0, 2.0)
     assert r_slow < r8
     # 2 GPUs of 1000 rows: 6000 ranked rows are read from the host already; replicating adds more: none
-    r2, _ = bench.replica_model(cum, total, 1000, 2, 737.0, 25.0, 6559.0)
+    r2, _ = bench.replica_model(cum, total, 1000, 2, 737.0, 25.0)
     assert r2 == 0
-    # everything cached and a fast host link: replicate until the HBM term binds, no further
+    # everything cached: replicate until the rows pushed out to the host cost what NVLink saves
     cum_all = np.concatenate([[0.0], np.cumsum(refs[:2000])])
-    r_all, rate_all = bench.replica_model(cum_all, float(cum_all[-1]), 1000, 2, 737.0, 1e9, 6559.0)
-    assert 0 < r_all < 1000 and abs(rate_all - 0.85 * 6559.0 / 2) < 1.0
+    r_all, rate_all = bench.replica_model(cum_all, float(cum_all[-1]), 1000, 2, 737.0, 25.0)
+    assert 0 < r_all < 1000 and rate_all > 0.86 * 737.0 / 0.5  # unreplicated: half the bytes remote
 
 
 def test_accumulator_merges_until_threshold(fake):
