@@ -242,6 +242,37 @@ def test_replica_model_trades_nvlink_for_host_reads():
     assert 0 < r_all < 1000 and rate_all > 0.86 * 737.0 / 0.5  # unreplicated: half the bytes remote
 
 
+def test_choose_replicas_end_to_end_on_cpu(monkeypatch):
+    """The bench's replica choice over pre-sampled minibatches (torch sampler on
+    the CPU, reference counts by bincount instead of the CUDA counting kernel):
+    'auto' returns rank 0's model choice, a number is clamped, 'off' is 0."""
+    import types
+
+    import bench
+    from GIDS import sampler as gs
+
+    monkeypatch.setattr(gs, "out_degree", lambda ids, n: torch.bincount(ids, minlength=n).to(torch.int32))
+    cfg = dict(bench.CONFIGS["c2"], nodes=20000, batch=64, torch_sampler=True)
+    _, ind = bench.graph_csc(cfg, "cpu")
+    hot = gs.top_rows(torch.bincount(ind.to(torch.int64), minlength=cfg["nodes"]).to(torch.int32), 8 * 1500)
+
+    class OneRank:
+        rank, world = 0, 1
+
+        def max(self, v):
+            return v
+
+    store = types.SimpleNamespace(geometry=lambda: {"cache_slots": 1500})
+    g = types.SimpleNamespace(BAM_FS=store, world=8)
+    args = types.SimpleNamespace(replicate="auto")
+    r = bench.choose_replicas(args, cfg, g, hot, "cpu", OneRank(), 1, 737.0, 25.0)
+    assert 0 <= r <= 1500
+    args.replicate = "100000"
+    assert bench.choose_replicas(args, cfg, g, hot, "cpu", OneRank(), 1, 737.0, 25.0) == 1500
+    args.replicate = "off"
+    assert bench.choose_replicas(args, cfg, g, hot, "cpu", OneRank(), 1, 737.0, 25.0) == 0
+
+
 def test_accumulator_merges_until_threshold(fake):
     g = fake(accumulator_flag=True)
     g.set_required_storage_access(bw=1.0, l_ssd=10, l_system=5, num_ssd=1, p=0.5)
