@@ -562,6 +562,8 @@ __global__ void __launch_bounds__(GATHER_THREADS, 2) gather_kernel(const __grid_
       const uint64_t pe = pb + psize, re = b0 + a.row_bytes;
       s1 = (uint32_t)((pe < re ? pe : re) - b0);
     }
+    // the shard that holds the line and its page-table entry there: line
+    // p % world at p / world, or a replicated line in this rank's own shard
     uint32_t owner = 0u;
     uint64_t lp = p;  // index in the owner's page table
     if (SYS) {
