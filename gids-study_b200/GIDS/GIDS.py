@@ -24,7 +24,6 @@ from __future__ import annotations
 
 import math
 import time
-from collections.abc import Mapping
 
 import torch
 

@@ -3,7 +3,6 @@ equals the oracle's stripe image (page_cache_backup.h:626-652, STRIPE), reads
 and writes go through the stripe map, capacity limits wrap, and the synthetic
 fill equals the oracle's generator."""
 import ctypes
-import os
 
 import numpy as np
 import pytest

@@ -4,7 +4,6 @@ handle exchange of a sharded GIDS (with a fake store recording what it got)."""
 import os
 import sys
 
-import pytest
 import torch.multiprocessing as mp
 
 HERE = os.path.dirname(os.path.abspath(__file__))
